@@ -1,0 +1,427 @@
+"""Benchmark of the B200 FFT path (batched 1D C2C, HBM GB/s).
+
+Workload (the north-star case): batched 1D complex64
+C2C FFT, N = 4096, batch = 65536 per GPU (2 GiB), re/im i.i.d. uniform[-1, 1)
+from a seeded generator. One step = one forward pass (x -> y) and one
+inverse pass with 1/N (y -> z) through the C ABI on device-resident buffers.
+The metric counts 16 bytes per complex element per pass (8 B read + 8 B
+write): GB/s = 2 * 16 * N * batch * ranks / step time. Every buffer (2 GiB)
+is larger than the 126 MB L2, so no L2 flush runs between steps.
+
+Multi-GPU (torchrun): one process per GPU, each transforming its own batch
+(weak scaling, no data-path collective); the timed region is bracketed by a
+barrier and device syncs and the time is the max over ranks.
+
+Arms:
+  default            this build's sm_100a kernels
+  --impl reference   the reference's CPU Stockham path, as restated in
+                     oracle/ (the Rust reference cannot be built here), on
+                     all host cores; rank 0 only.
+
+Extra keys on the JSON line: roofline (dominant kernel, per-launch CUDA
+events in the timed region vs the measured HBM copy bandwidth), cpu_baseline
+(the oracle on a bounded sample), e2e (the public host-pointer API with
+pinned buffers, copies inside the timed region), clocks (nvidia-smi sampled
+during the timed region) and gpu_launches.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "ferrum-gpu_b200"))
+sys.path.insert(0, REPO)
+
+METRIC = "batched 1D C2C FFT HBM GB/s"
+UNIT = "GB/s"
+LOG_N = 12
+BATCH = 65536
+BYTES_PER_ELEM_PASS = 16
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="transforms per GPU (default 65536 = 2 GiB; smaller only for profiling)")
+    return ap.parse_args()
+
+
+def workload_config(batch: int) -> dict:
+    return {
+        "workload": f"batched 1D C2C forward+inverse(1/N), N={1 << LOG_N}, batch={batch} per GPU "
+                    f"({(batch << LOG_N) * 8 / 2**30:g} GiB complex64), one step = 2 passes",
+        "n": 1 << LOG_N,
+        "batch_per_gpu": batch,
+        "inputs": "re/im i.i.d. uniform[-1,1), seeded",
+        "l2": f"no flush: every buffer is {(batch << LOG_N) * 8 / 2**20:g} MiB > 126 MB L2",
+        "bytes_counted": "16 B per complex element per pass",
+    }
+
+
+def measured_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/fft_rows_kernel_4096x65536.md), if present."""
+    path = os.path.join(REPO, "profiles", "fft_rows_kernel_4096x65536.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except Exception:
+        pass
+    return None
+
+
+# --------------------------------------------------------------------------
+# CPU side (oracle) — test/baseline infrastructure only.
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def time_oracle(transforms: int, threads: int, seed: int = 0):
+    """Forward + inverse(1/N) of `transforms` lanes with the oracle; returns
+    (seconds, bytes counted)."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(seed)
+    n = 1 << LOG_N
+    x = (rng.uniform(-1, 1, transforms * n) + 1j * rng.uniform(-1, 1, transforms * n)).astype(
+        np.complex64)
+    t0 = time.perf_counter()
+    y = oracle.fft_1d(x, LOG_N, "forward", False, threads=threads)
+    oracle.fft_1d(y, LOG_N, "inverse", True, threads=threads)
+    dt = time.perf_counter() - t0
+    return dt, 2 * BYTES_PER_ELEM_PASS * n * transforms
+
+
+def calibrate_oracle(threads: int) -> float:
+    """Seconds per transform (fwd + inv) of the oracle on `threads` threads."""
+    probe = max(threads * 4, 64)
+    dt, _ = time_oracle(probe, threads, seed=1)
+    return dt / probe
+
+
+def cpu_baseline_leg(target_seconds: float) -> dict:
+    threads = host_cores()
+    per = calibrate_oracle(threads)
+    sample = max(threads, int(target_seconds / max(per, 1e-9)))
+    sample = min(sample, BATCH)
+    dt, nbytes = time_oracle(sample, threads, seed=2)
+    return {
+        "value": round(nbytes / dt / 1e9, 3),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{sample} of the {BATCH} transforms (N={1 << LOG_N}), forward+inverse, "
+                  f"lane-parallel oracle (C restatement of crates/ferrum-gpu-fft/src/cpu.rs) "
+                  f"on {threads} threads, {cpu_model()}; {dt:.1f} s",
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    threads = host_cores()
+    per = calibrate_oracle(threads)
+    budget = 90.0
+    sample = int(budget / max(per, 1e-9) / max(1, args.steps + args.warmup))
+    sample = max(threads, min(sample, BATCH))
+    for w in range(args.warmup):
+        time_oracle(sample, threads, seed=100 + w)
+    total_t = 0.0
+    total_b = 0
+    for k in range(args.steps):
+        dt, nb = time_oracle(sample, threads, seed=200 + k)
+        total_t += dt
+        total_b += nb
+    value = total_b / total_t / 1e9
+    sample_desc = (f"{sample} of the {BATCH} transforms per step (N={1 << LOG_N}), "
+                   f"forward+inverse(1/N), lane-parallel oracle port of "
+                   f"crates/ferrum-gpu-fft/src/cpu.rs on {threads} threads, {cpu_model()}")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total_t / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": workload_config(BATCH),
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
+                         "kind": "port", "sample": sample_desc},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the Rust/cuda-oxide reference cannot be built in this image (no cargo, no "
+                "network); its CPU Stockham path is timed through the C restatement in oracle/",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU side.
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,"
+             "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 10]
+        loaded = []
+        reasons = set()
+        max_mhz = None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm, smax, util = float(r[1]), float(r[2]), float(r[3])
+            except ValueError:
+                continue
+            max_mhz = smax
+            if util >= 50:
+                loaded.append(sm)
+                for name, v in zip(names, r[6:10]):
+                    if v.strip().lower() == "active":
+                        reasons.add(name)
+        samples = loaded or [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(samples) if samples else None,
+                "sm_max_mhz": max_mhz, "reasons": sorted(reasons),
+                "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from ferrum_gpu import capi
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B_ = args.batch
+    dev = capi.DeviceHandle(local)
+    n = 1 << LOG_N
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    x = torch.complex(torch.rand(B_, n, device="cuda", generator=g) * 2 - 1,
+                      torch.rand(B_, n, device="cuda", generator=g) * 2 - 1)
+    y = torch.empty_like(x)
+    z = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    launches_per_step = 2 * capi.launch_count(LOG_N, B_, 1)
+
+    def step(events=None):
+        if events is not None:
+            events[0].record(stream)
+        capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), LOG_N, B_, "forward", False, sp)
+        if events is not None:
+            events[1].record(stream)
+            events[2].record(stream)
+        capi.fft_1d(dev, y.data_ptr(), z.data_ptr(), LOG_N, B_, "inverse", True, sp)
+        if events is not None:
+            events[3].record(stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    # correctness gate on the measured buffers: inverse(forward(x)) == x
+    err = float((z - x).abs().max() / x.abs().max())
+    if err > 1e-4:
+        raise SystemExit(f"round-trip error {err} exceeds 1e-4; refusing to report")
+
+    per_launch = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                  for _ in range(args.steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for k in range(args.steps):
+        step(per_launch[k])
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end))
+    launch_ms = [ev[0].elapsed_time(ev[1]) for ev in per_launch] + \
+                [ev[2].elapsed_time(ev[3]) for ev in per_launch]
+    avg_launch_ms = max_over_ranks(sum(launch_ms) / len(launch_ms))
+
+    bytes_per_pass = BYTES_PER_ELEM_PASS * n * B_
+    value = world * args.steps * 2 * bytes_per_pass / (elapsed_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    achieved = bytes_per_pass / (avg_launch_ms * 1e-3) / 1e9
+    traffic = profiled_traffic()
+
+    # End to end through the public host-pointer API with pinned buffers.
+    e2e = None
+    if not args.no_e2e:
+        hx = x.cpu().pin_memory()
+        hy = torch.empty_like(hx).pin_memory()
+        hz = torch.empty_like(hx).pin_memory()
+        capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), LOG_N, B_, "forward", False)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), LOG_N, B_, "forward", False)
+            capi.fft_1d_host(dev, hy.data_ptr(), hz.data_ptr(), LOG_N, B_, "inverse", True)
+        t_e2e = max_over_ranks(time.perf_counter() - t0)
+        barrier()
+        e2e_err = float((hz - hx).abs().max() / hx.abs().max())
+        if e2e_err > 1e-4:
+            raise SystemExit(f"e2e round-trip error {e2e_err} exceeds 1e-4")
+        e2e = {"value": round(world * args.e2e_steps * 2 * bytes_per_pass / t_e2e / 1e9, 3),
+               "unit": UNIT,
+               "h2d_bytes_per_step": 2 * 8 * n * B_,
+               "d2h_bytes_per_step": 2 * 8 * n * B_,
+               "steps": args.e2e_steps,
+               "path": "ferrum_fft_1d_c2c_pow2_host (C ABI), pinned host buffers, forward + inverse"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_leg(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(elapsed_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": workload_config(B_),
+            "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
+            "transforms_per_s": round(world * args.steps * 2 * B_ / (elapsed_ms * 1e-3), 1),
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "fft_rows_kernel<12,4,1,*,*> (single-pass N=4096)",
+                "achieved": round(achieved, 2),
+                "peak": peak,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
+                "measured" else "fallback 6.65 TB/s",
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": bytes_per_pass,
+                "avg_launch_ms": round(avg_launch_ms, 5),
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": args.steps * launches_per_step,
+            "roundtrip_max_rel_err": err,
+        }
+        print(json.dumps(line), flush=True)
+    dev.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,368 @@
+// Runtime and C ABI of the B200 FFT path (include/ferrum_fft.h).
+//
+// The device handle replaces the reference's persistent `Device` (a CUDA
+// context plus a loaded PTX module, crates/ferrum-gpu-py/src/lib.rs:389-417):
+// here it owns every twiddle table, uploaded once, and a stream-ordered
+// memory pool for four-step workspaces. The reference instead rebuilt and
+// re-uploaded its twiddles, allocated input/output/twiddle buffers and
+// conjugated on the host on every call (lib.rs:105-140, :237-247).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "fft_kernels.cuh"
+#include "fft_launch.h"
+#include "runtime.h"
+#include "twiddle_tables.h"
+
+#define FERRUM_VERSION "0.3.0-b200"
+
+namespace ferrum {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+ferrum_status set_error(ferrum_status code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+ferrum_status cuda_error(cudaError_t e, const char* what) {
+  return set_error(FERRUM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                                        cudaGetErrorString(e) + ")");
+}
+
+void clear_error() { g_last_error.clear(); }
+
+DeviceGuard::DeviceGuard(int ordinal) {
+  if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+  if (prev_ != ordinal) status_ = cudaSetDevice(ordinal);
+}
+
+DeviceGuard::~DeviceGuard() {
+  int cur = -1;
+  if (prev_ >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev_) cudaSetDevice(prev_);
+}
+
+const float2* stage_table(const ferrum_device* dev, int log_n) {
+  return dev->tables + dev->stage_off[log_n];
+}
+const float2* tw4_lo_table(const ferrum_device* dev, int log_n) {
+  return dev->tables + dev->tw4_lo_off[log_n];
+}
+const float2* tw4_hi_table(const ferrum_device* dev, int log_n) {
+  return dev->tables + dev->tw4_hi_off[log_n];
+}
+
+namespace {
+
+bool valid_direction(int direction) { return direction == 1 || direction == -1; }
+
+ferrum_status check_device(const ferrum_device* dev) {
+  if (dev == nullptr || dev->tables == nullptr)
+    return set_error(FERRUM_ERR_INVALID_ARG, "device handle is NULL or destroyed");
+  return FERRUM_OK;
+}
+
+ferrum_status check_common(int log_n, int lo, int hi, size_t batch, int direction,
+                           const char* what) {
+  if (log_n < lo || log_n > hi)
+    return set_error(FERRUM_ERR_INVALID_ARG, std::string(what) + ": log_n must be in [" +
+                                                 std::to_string(lo) + ", " + std::to_string(hi) +
+                                                 "], got " + std::to_string(log_n));
+  if (batch == 0)
+    return set_error(FERRUM_ERR_INVALID_ARG, std::string(what) + ": batch must be positive");
+  if (!valid_direction(direction))
+    return set_error(FERRUM_ERR_INVALID_ARG,
+                     std::string(what) + ": direction must be +1 (forward) or -1 (inverse), got " +
+                         std::to_string(direction));
+  return FERRUM_OK;
+}
+
+bool is_aligned8(const void* p) { return ((uintptr_t)p & 7u) == 0; }
+
+}  // namespace
+
+size_t workspace_1d_bytes(int log_n, int64_t batch) {
+  if (log_n <= kMaxSinglePassLogN) return 0;
+  return ((size_t)1 << log_n) * (size_t)batch * sizeof(float2);
+}
+
+ferrum_status enqueue_1d(ferrum_device* dev, const float2* in, float2* out, int log_n,
+                         int64_t batch, int direction, bool normalize, float2* ws,
+                         cudaStream_t stream) {
+  const bool inv = direction < 0;
+  const float scale = (inv && normalize) ? 1.0f / (float)((int64_t)1 << log_n) : 1.0f;
+  cudaError_t e;
+  if (log_n <= kMaxSinglePassLogN) {
+    e = launch_rows(log_n, inv, inv, in, out, stage_table(dev, log_n), batch, scale, stream);
+    if (e != cudaSuccess) return cuda_error(e, "fft_rows_kernel launch");
+    return FERRUM_OK;
+  }
+  // Four-step: x as N1 rows x N2 columns; pass A = column FFTs with the
+  // W_N^(n2*k1) twiddle fused into the store, pass B = row FFTs stored
+  // transposed so that X[k1 + N1*k2] lands in natural order.
+  const int l1 = four_step_log_n1(log_n), l2 = four_step_log_n2(log_n);
+  const int64_t n = (int64_t)1 << log_n;
+  ColsArgs a{};
+  a.nfft = batch << l2;
+  a.img_stride = n;
+  a.ld = (int64_t)1 << l2;
+  a.log_cols = l2;
+  a.scale = 1.0f;
+  a.tw4_lo = tw4_lo_table(dev, log_n);
+  a.tw4_hi = tw4_hi_table(dev, log_n);
+  e = launch_cols(l1, inv, false, true, in, ws, stage_table(dev, l1), a, stream);
+  if (e != cudaSuccess) return cuda_error(e, "four-step pass A launch");
+  RowsTArgs b{};
+  b.nfft = batch << l1;
+  b.log_rows = l1;
+  b.scale = scale;
+  e = launch_rows_t(l2, inv, ws, out, stage_table(dev, l2), b, stream);
+  if (e != cudaSuccess) return cuda_error(e, "four-step pass B launch");
+  return FERRUM_OK;
+}
+
+ferrum_status enqueue_2d(ferrum_device* dev, const float2* in, float2* out, int log_n,
+                         int64_t batch, int direction, bool normalize, cudaStream_t stream) {
+  const bool inv = direction < 0;
+  const int64_t n = (int64_t)1 << log_n;
+  // cpu_2d.rs:56-62: one 1/(n*n) scale computed in float.
+  const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
+  const float2* tw = stage_table(dev, log_n);
+  cudaError_t e = launch_rows(log_n, inv, false, in, out, tw, batch * n, 1.0f, stream);
+  if (e != cudaSuccess) return cuda_error(e, "2D row pass launch");
+  ColsArgs a{};
+  a.nfft = batch * n;
+  a.img_stride = n * n;
+  a.ld = n;
+  a.log_cols = log_n;
+  a.scale = scale;
+  e = launch_cols(log_n, false, inv, false, out, out, tw, a, stream);
+  if (e != cudaSuccess) return cuda_error(e, "2D column pass launch");
+  return FERRUM_OK;
+}
+
+}  // namespace ferrum
+
+using namespace ferrum;
+
+extern "C" {
+
+const char* ferrum_version(void) { return FERRUM_VERSION; }
+
+const char* ferrum_last_error(void) { return g_last_error.c_str(); }
+
+ferrum_status ferrum_device_create(int ordinal, ferrum_device** out) {
+  clear_error();
+  if (out == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDeviceCount");
+  if (ordinal < 0 || ordinal >= count)
+    return set_error(FERRUM_ERR_INVALID_ARG, "device ordinal " + std::to_string(ordinal) +
+                                                 " out of range (" + std::to_string(count) +
+                                                 " devices)");
+  DeviceGuard guard(ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, ordinal);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDeviceProperties");
+  if (prop.major != 10 || prop.minor != 0)
+    return set_error(FERRUM_ERR_UNSUPPORTED,
+                     std::string("ferrum-gpu kernels are built for sm_100a (B200); device is ") +
+                         prop.name + " sm_" + std::to_string(prop.major) +
+                         std::to_string(prop.minor));
+
+  std::vector<float2> host;
+  auto* dev = new ferrum_device();
+  dev->ordinal = ordinal;
+  for (int l = 0; l <= kMaxSinglePassLogN; ++l) dev->stage_off[l] = -1;
+  for (int l = 0; l <= kMaxLogN; ++l) dev->tw4_lo_off[l] = dev->tw4_hi_off[l] = -1;
+  for (int l = 2; l <= kMaxSinglePassLogN; ++l) {
+    dev->stage_off[l] = (int64_t)host.size();
+    append_stage_tables(host, l);
+    host.push_back(make_float2(1.f, 0.f));  // keeps every offset valid for 1-stage plans
+  }
+  for (int l = kMaxSinglePassLogN + 1; l <= kMaxLogN; ++l) {
+    std::vector<float2> lo, hi;
+    append_four_step_tables(lo, hi, l);
+    dev->tw4_lo_off[l] = (int64_t)host.size();
+    host.insert(host.end(), lo.begin(), lo.end());
+    dev->tw4_hi_off[l] = (int64_t)host.size();
+    host.insert(host.end(), hi.begin(), hi.end());
+  }
+  dev->table_entries = host.size();
+  e = cudaMalloc(&dev->tables, host.size() * sizeof(float2));
+  if (e != cudaSuccess) {
+    delete dev;
+    return cuda_error(e, "cudaMalloc(twiddle tables)");
+  }
+  e = cudaMemcpy(dev->tables, host.data(), host.size() * sizeof(float2), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(dev->tables);
+    delete dev;
+    return cuda_error(e, "cudaMemcpy(twiddle tables)");
+  }
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.handleTypes = cudaMemHandleTypeNone;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = ordinal;
+  e = cudaMemPoolCreate(&dev->pool, &props);
+  if (e != cudaSuccess) {
+    cudaFree(dev->tables);
+    delete dev;
+    return cuda_error(e, "cudaMemPoolCreate");
+  }
+  uint64_t keep = UINT64_MAX;
+  cudaMemPoolSetAttribute(dev->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  *out = dev;
+  return FERRUM_OK;
+}
+
+ferrum_status ferrum_device_destroy(ferrum_device* dev) {
+  clear_error();
+  if (dev == nullptr) return FERRUM_OK;
+  DeviceGuard guard(dev->ordinal);
+  cudaDeviceSynchronize();
+  for (int i = 0; i < ferrum_device::kHostStreams; ++i) {
+    if (dev->host_streams[i]) cudaStreamDestroy(dev->host_streams[i]);
+    if (dev->host_dbuf[i]) cudaFree(dev->host_dbuf[i]);
+    if (dev->host_ws[i]) cudaFree(dev->host_ws[i]);
+    if (dev->host_pin_in[i]) cudaFreeHost(dev->host_pin_in[i]);
+    if (dev->host_pin_out[i]) cudaFreeHost(dev->host_pin_out[i]);
+  }
+  if (dev->pool) cudaMemPoolDestroy(dev->pool);
+  if (dev->tables) cudaFree(dev->tables);
+  dev->tables = nullptr;
+  delete dev;
+  return FERRUM_OK;
+}
+
+ferrum_status ferrum_device_sync(ferrum_device* dev) {
+  clear_error();
+  if (ferrum_status s = check_device(dev)) return s;
+  DeviceGuard guard(dev->ordinal);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_error(e, "cudaDeviceSynchronize");
+  return FERRUM_OK;
+}
+
+ferrum_status ferrum_device_ordinal(const ferrum_device* dev, int* ordinal) {
+  clear_error();
+  if (ferrum_status s = check_device(dev)) return s;
+  if (ordinal == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, "ordinal is NULL");
+  *ordinal = dev->ordinal;
+  return FERRUM_OK;
+}
+
+ferrum_status ferrum_fft_workspace_bytes(int log_n, size_t batch, int kind, size_t* bytes) {
+  clear_error();
+  if (bytes == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, "bytes is NULL");
+  if (kind == 1) {
+    if (ferrum_status s = check_common(log_n, 2, kMaxLogN, batch, 1, "workspace")) return s;
+    *bytes = workspace_1d_bytes(log_n, (int64_t)batch);
+    return FERRUM_OK;
+  }
+  if (kind == 2) {
+    if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "workspace"))
+      return s;
+    *bytes = 0;
+    return FERRUM_OK;
+  }
+  return set_error(FERRUM_ERR_INVALID_ARG, "kind must be 1 (1D) or 2 (2D)");
+}
+
+ferrum_status ferrum_fft_launch_count(int log_n, size_t batch, int kind, int* launches) {
+  clear_error();
+  if (launches == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, "launches is NULL");
+  if (kind == 1) {
+    if (ferrum_status s = check_common(log_n, 2, kMaxLogN, batch, 1, "launch_count")) return s;
+    *launches = log_n <= kMaxSinglePassLogN ? 1 : 2;
+    return FERRUM_OK;
+  }
+  if (kind == 2) {
+    if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "launch_count"))
+      return s;
+    *launches = 2;
+    return FERRUM_OK;
+  }
+  return set_error(FERRUM_ERR_INVALID_ARG, "kind must be 1 (1D) or 2 (2D)");
+}
+
+ferrum_status ferrum_fft_1d_c2c_pow2_ws(ferrum_device* dev, const void* in_dev, void* out_dev,
+                                        int log_n, size_t batch, int direction, int normalize,
+                                        void* workspace_dev, size_t workspace_bytes,
+                                        void* stream) {
+  clear_error();
+  if (ferrum_status s = check_device(dev)) return s;
+  if (ferrum_status s = check_common(log_n, 2, kMaxLogN, batch, direction, "fft_1d_c2c_pow2"))
+    return s;
+  if (in_dev == nullptr || out_dev == nullptr)
+    return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2: in/out is NULL");
+  if (!is_aligned8(in_dev) || !is_aligned8(out_dev))
+    return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2: in/out must be 8-byte aligned");
+  const size_t need = workspace_1d_bytes(log_n, (int64_t)batch);
+  if (need > 0 && (workspace_dev == nullptr || workspace_bytes < need))
+    return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2: workspace needs " +
+                                                 std::to_string(need) + " bytes");
+  if (need > 0 && !is_aligned8(workspace_dev))
+    return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2: workspace must be 8-byte aligned");
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  return enqueue_1d(dev, (const float2*)in_dev, (float2*)out_dev, log_n, (int64_t)batch,
+                    direction, normalize != 0, (float2*)workspace_dev, (cudaStream_t)stream);
+}
+
+ferrum_status ferrum_fft_1d_c2c_pow2(ferrum_device* dev, const void* in_dev, void* out_dev,
+                                     int log_n, size_t batch, int direction, int normalize,
+                                     void* stream) {
+  clear_error();
+  if (ferrum_status s = check_device(dev)) return s;
+  if (ferrum_status s = check_common(log_n, 2, kMaxLogN, batch, direction, "fft_1d_c2c_pow2"))
+    return s;
+  const size_t need = workspace_1d_bytes(log_n, (int64_t)batch);
+  if (need == 0)
+    return ferrum_fft_1d_c2c_pow2_ws(dev, in_dev, out_dev, log_n, batch, direction, normalize,
+                                     nullptr, 0, stream);
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  void* ws = nullptr;
+  cudaError_t e = cudaMallocFromPoolAsync(&ws, need, dev->pool, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMallocFromPoolAsync(workspace)");
+  ferrum_status s = ferrum_fft_1d_c2c_pow2_ws(dev, in_dev, out_dev, log_n, batch, direction,
+                                              normalize, ws, need, stream);
+  e = cudaFreeAsync(ws, (cudaStream_t)stream);
+  if (s == FERRUM_OK && e != cudaSuccess) return cuda_error(e, "cudaFreeAsync(workspace)");
+  return s;
+}
+
+ferrum_status ferrum_fft_2d_c2c_pow2(ferrum_device* dev, const void* in_dev, void* out_dev,
+                                     int log_n, size_t batch, int direction, int normalize,
+                                     void* stream) {
+  clear_error();
+  if (ferrum_status s = check_device(dev)) return s;
+  if (ferrum_status s =
+          check_common(log_n, 2, kMaxSinglePassLogN, batch, direction, "fft_2d_c2c_pow2"))
+    return s;
+  if (in_dev == nullptr || out_dev == nullptr)
+    return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2: in/out is NULL");
+  if (!is_aligned8(in_dev) || !is_aligned8(out_dev))
+    return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2: in/out must be 8-byte aligned");
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  return enqueue_2d(dev, (const float2*)in_dev, (float2*)out_dev, log_n, (int64_t)batch,
+                    direction, normalize != 0, (cudaStream_t)stream);
+}
+
+}  // extern "C"

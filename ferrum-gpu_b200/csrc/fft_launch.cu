@@ -1,0 +1,214 @@
+// Template dispatch from runtime (log_n, direction flags) to the pass kernels.
+#include <atomic>
+
+#include "fft_kernels.cuh"
+#include "fft_launch.h"
+
+namespace ferrum {
+namespace {
+
+constexpr int kRowsThreads = 256;   // batched rows: 256 threads per CTA up to N = 4096
+constexpr int kColsThreads = 512;   // strided passes: up to 16 columns / rows per CTA
+
+constexpr int rows_fpb(int log_n) {
+  return (plan_log_p(log_n) == log_n || (1 << (log_n - plan_log_p(log_n))) <= kRowsThreads)
+             ? kRowsThreads / (1 << (log_n - plan_log_p(log_n)))
+             : 1;
+}
+constexpr int cols_fpb(int log_n) {
+  // clamp(512 / T, 1, 16)
+  return (kColsThreads >> (log_n - plan_log_p(log_n))) < 1
+             ? 1
+             : ((kColsThreads >> (log_n - plan_log_p(log_n))) > 16
+                    ? 16
+                    : (kColsThreads >> (log_n - plan_log_p(log_n))));
+}
+
+// Raise the dynamic shared-memory limit once per (kernel, device).
+template <class K>
+cudaError_t ensure_smem(K kernel, size_t bytes) {
+  static std::atomic<uint64_t> done{0};
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+template <int LOGN, bool CI, bool CO>
+cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t nfft, float scale,
+                      int log_block, cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = rows_fpb(LOGN);
+  using C = RowsCfg<LOGN, LOGP, FPB, CI, CO>;
+  auto k = fft_rows_kernel<LOGN, LOGP, FPB, CI, CO>;
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = ceil_div(nfft, FPB);
+  k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, log_block);
+  return cudaGetLastError();
+}
+
+template <int LOGN, bool CI, bool CO, bool TW>
+cudaError_t cols_impl(const float2* in, float2* out, const float2* tw, const ColsArgs& a,
+                      cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = cols_fpb(LOGN);
+  using C = ColsCfg<LOGN, LOGP, FPB, CI, CO, TW>;
+  auto k = fft_cols_kernel<LOGN, LOGP, FPB, CI, CO, TW>;
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = ceil_div(a.nfft, FPB);
+  k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);
+  return cudaGetLastError();
+}
+
+template <int LOGN, bool CO>
+cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const RowsTArgs& a,
+                        cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = cols_fpb(LOGN);
+  using C = RowsTCfg<LOGN, LOGP, FPB, CO>;
+  auto k = fft_rows_t_kernel<LOGN, LOGP, FPB, CO>;
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = ceil_div(a.nfft, FPB);
+  k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);
+  return cudaGetLastError();
+}
+
+template <int LOGN>
+cudaError_t rows_dispatch(bool ci, bool co, const float2* in, float2* out, const float2* tw,
+                          int64_t nfft, float scale, int lb, cudaStream_t s) {
+  if (ci && co) return rows_impl<LOGN, true, true>(in, out, tw, nfft, scale, lb, s);
+  if (ci) return rows_impl<LOGN, true, false>(in, out, tw, nfft, scale, lb, s);
+  if (co) return rows_impl<LOGN, false, true>(in, out, tw, nfft, scale, lb, s);
+  return rows_impl<LOGN, false, false>(in, out, tw, nfft, scale, lb, s);
+}
+
+template <int LOGN>
+cudaError_t cols_dispatch(bool ci, bool co, bool tw4, const float2* in, float2* out,
+                          const float2* tw, const ColsArgs& a, cudaStream_t s) {
+  if (tw4) {
+    if constexpr (LOGN >= 7 && LOGN <= 13) {
+      if (co) return cudaErrorInvalidValue;  // four-step pass A never conjugates its output
+      if (ci) return cols_impl<LOGN, true, false, true>(in, out, tw, a, s);
+      return cols_impl<LOGN, false, false, true>(in, out, tw, a, s);
+    } else {
+      return cudaErrorInvalidValue;
+    }
+  }
+  if (ci && co) return cols_impl<LOGN, true, true, false>(in, out, tw, a, s);
+  if (ci) return cols_impl<LOGN, true, false, false>(in, out, tw, a, s);
+  if (co) return cols_impl<LOGN, false, true, false>(in, out, tw, a, s);
+  return cols_impl<LOGN, false, false, false>(in, out, tw, a, s);
+}
+
+template <int LOGN>
+cudaError_t rows_t_dispatch(bool co, const float2* in, float2* out, const float2* tw,
+                            const RowsTArgs& a, cudaStream_t s) {
+  if (co) return rows_t_impl<LOGN, true>(in, out, tw, a, s);
+  return rows_t_impl<LOGN, false>(in, out, tw, a, s);
+}
+
+
+// out[r][p*bw + c] = in[p][r][c]; one thread moves two complex values.
+__global__ void __launch_bounds__(256) block_gather_kernel(const float4* __restrict__ in,
+                                                           float4* __restrict__ out,
+                                                           int64_t total2, int64_t rows,
+                                                           int64_t bw2) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total2; i += stride) {
+    const int64_t c = i % bw2;
+    const int64_t r = (i / bw2) % rows;
+    const int64_t p = i / (bw2 * rows);
+    const int64_t nblocks = total2 / (bw2 * rows);
+    out[r * (nblocks * bw2) + p * bw2 + c] = __ldcs(in + i);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, int64_t rows,
+                                int64_t bw, cudaStream_t stream) {
+  if (bw % 2 != 0 || ((uintptr_t)in & 15) || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
+  const int64_t total2 = nblocks * rows * bw / 2;
+  int64_t grid = (total2 + 255) / 256;
+  if (grid > 148 * 32) grid = 148 * 32;
+  if (grid < 1) grid = 1;
+  block_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>((const float4*)in, (float4*)out, total2,
+                                                          rows, bw / 2);
+  return cudaGetLastError();
+}
+
+#define FERRUM_CASE_2_14(X) \
+  X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
+
+cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
+                        const float2* tw, int64_t nfft, float scale, cudaStream_t stream,
+                        int log_block) {
+  if (log_block < 0 || log_block > log_n) log_block = log_n;
+  switch (log_n) {
+#define X(L) \
+  case L:    \
+    return rows_dispatch<L>(conj_in, conj_out, in, out, tw, nfft, scale, log_block, stream);
+    FERRUM_CASE_2_14(X)
+#undef X
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+LaunchShape rows_shape(int log_n, int64_t nfft) {
+  const int lp = plan_log_p(log_n);
+  const int t = 1 << (log_n - lp);
+  const int fpb = t <= kRowsThreads ? kRowsThreads / t : 1;
+  const int stride = (1 << log_n) + ((1 << log_n) >> 4) + 16;
+  return LaunchShape{ceil_div(nfft, fpb), fpb * t,
+                     plan_num_stages(log_n, lp) > 1 ? (size_t)fpb * stride * 8 : 0};
+}
+
+cudaError_t launch_cols(int log_n, bool conj_in, bool conj_out, bool tw4, const float2* in,
+                        float2* out, const float2* tw, const ColsArgs& args, cudaStream_t stream) {
+  switch (log_n) {
+#define X(L) \
+  case L:    \
+    return cols_dispatch<L>(conj_in, conj_out, tw4, in, out, tw, args, stream);
+    FERRUM_CASE_2_14(X)
+#undef X
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+LaunchShape cols_shape(int log_n, int64_t nfft) {
+  const int lp = plan_log_p(log_n);
+  const int t = 1 << (log_n - lp);
+  int fpb = kColsThreads / t;
+  fpb = fpb < 1 ? 1 : (fpb > 16 ? 16 : fpb);
+  const int stride = (1 << log_n) + ((1 << log_n) >> 4) + 16;
+  return LaunchShape{ceil_div(nfft, fpb), fpb * t, (size_t)fpb * stride * 8};
+}
+
+cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* out,
+                          const float2* tw, const RowsTArgs& args, cudaStream_t stream) {
+  switch (log_n) {
+#define X(L) \
+  case L:    \
+    return rows_t_dispatch<L>(conj_out, in, out, tw, args, stream);
+    X(8) X(9) X(10) X(11) X(12) X(13)
+#undef X
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+LaunchShape rows_t_shape(int log_n, int64_t nfft) { return cols_shape(log_n, nfft); }
+
+}  // namespace ferrum

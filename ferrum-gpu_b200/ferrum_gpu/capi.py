@@ -1,0 +1,173 @@
+"""ctypes binding of the C ABI in include/ferrum_fft.h.
+
+This is the binding a caller of the reference would add to reach the B200
+kernels through plain pointers: device-resident buffers (for example
+``torch.Tensor.data_ptr()`` of a CUDA complex64 tensor), a ``cudaStream_t``
+and sizes. Every function raises :class:`FerrumError` with the library's
+status code and ``ferrum_last_error()`` message on failure. There is no CPU
+fallback: on a machine without a B200 the compute calls fail with
+``FERRUM_ERR_CUDA`` / ``FERRUM_ERR_UNSUPPORTED``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libferrum_fft.so")
+
+FERRUM_OK = 0
+FERRUM_ERR_INVALID_ARG = 1
+FERRUM_ERR_CUDA = 2
+FERRUM_ERR_NCCL = 3
+FERRUM_ERR_TIMEOUT = 4
+FERRUM_ERR_ALLOC = 5
+FERRUM_ERR_UNSUPPORTED = 6
+FORWARD = 1
+INVERSE = -1
+DIST_ID_BYTES = 128
+
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_i = ctypes.c_int
+
+# name -> (restype, argtypes); mirrors include/ferrum_fft.h one to one.
+SIGNATURES = {
+    "ferrum_version": (ctypes.c_char_p, []),
+    "ferrum_last_error": (ctypes.c_char_p, []),
+    "ferrum_device_create": (_i, [_i, ctypes.POINTER(_vp)]),
+    "ferrum_device_destroy": (_i, [_vp]),
+    "ferrum_device_sync": (_i, [_vp]),
+    "ferrum_device_ordinal": (_i, [_vp, ctypes.POINTER(_i)]),
+    "ferrum_fft_1d_c2c_pow2": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
+    "ferrum_fft_1d_c2c_pow2_ws": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp, _sz, _vp]),
+    "ferrum_fft_2d_c2c_pow2": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
+    "ferrum_fft_1d_c2c_pow2_host": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i]),
+    "ferrum_fft_2d_c2c_pow2_host": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i]),
+    "ferrum_fft_workspace_bytes": (_i, [_i, _sz, _i, ctypes.POINTER(_sz)]),
+    "ferrum_fft_launch_count": (_i, [_i, _sz, _i, ctypes.POINTER(_i)]),
+    "ferrum_dist_get_unique_id": (_i, [ctypes.c_char_p]),
+    "ferrum_dist_init": (_i, [_vp, ctypes.c_char_p, _i, _i, _i, ctypes.POINTER(_vp)]),
+    "ferrum_dist_destroy": (_i, [_vp]),
+    "ferrum_dist_world": (_i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "ferrum_dist_workspace_bytes": (_i, [_vp, _i, ctypes.POINTER(_sz)]),
+    "ferrum_fft_2d_c2c_pow2_dist": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "ferrum_dist_sync": (_i, [_vp, _vp]),
+    "ferrum_dist_check": (_i, [_i, _i]),
+}
+
+
+class FerrumError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"ferrum status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libferrum_fft.so (raises if the library has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python ferrum-gpu_b200/build.py`")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    return lib().ferrum_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != FERRUM_OK:
+        raise FerrumError(status, last_error())
+
+
+def version() -> str:
+    return lib().ferrum_version().decode()
+
+
+class DeviceHandle:
+    """Owning wrapper of a ``ferrum_device*``."""
+
+    def __init__(self, ordinal: int = 0):
+        h = _vp()
+        check(lib().ferrum_device_create(ordinal, ctypes.byref(h)))
+        self.ptr = h
+        self.ordinal = ordinal
+
+    def sync(self) -> None:
+        check(lib().ferrum_device_sync(self.ptr))
+
+    def close(self) -> None:
+        if self.ptr:
+            lib().ferrum_device_destroy(self.ptr)
+            self.ptr = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _dir(direction) -> int:
+    if direction in (1, "forward"):
+        return FORWARD
+    if direction in (-1, "inverse"):
+        return INVERSE
+    raise ValueError(f"direction must be 'forward' or 'inverse', got {direction!r}")
+
+
+def fft_1d(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: int,
+           direction="forward", normalize: bool = False, stream: int = 0) -> None:
+    """Enqueue a batched 1D C2C transform on device pointers."""
+    check(lib().ferrum_fft_1d_c2c_pow2(dev.ptr, in_ptr, out_ptr, log_n, batch, _dir(direction),
+                                       int(bool(normalize)), stream))
+
+
+def fft_1d_ws(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: int,
+              direction, normalize: bool, ws_ptr: int, ws_bytes: int, stream: int = 0) -> None:
+    check(lib().ferrum_fft_1d_c2c_pow2_ws(dev.ptr, in_ptr, out_ptr, log_n, batch,
+                                          _dir(direction), int(bool(normalize)), ws_ptr,
+                                          ws_bytes, stream))
+
+
+def fft_2d(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: int,
+           direction="forward", normalize: bool = False, stream: int = 0) -> None:
+    """Enqueue a batched 2D C2C transform on device pointers."""
+    check(lib().ferrum_fft_2d_c2c_pow2(dev.ptr, in_ptr, out_ptr, log_n, batch, _dir(direction),
+                                       int(bool(normalize)), stream))
+
+
+def fft_1d_host(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: int,
+                direction="forward", normalize: bool = False) -> None:
+    check(lib().ferrum_fft_1d_c2c_pow2_host(dev.ptr, in_ptr, out_ptr, log_n, batch,
+                                            _dir(direction), int(bool(normalize))))
+
+
+def fft_2d_host(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: int,
+                direction="forward", normalize: bool = False) -> None:
+    check(lib().ferrum_fft_2d_c2c_pow2_host(dev.ptr, in_ptr, out_ptr, log_n, batch,
+                                            _dir(direction), int(bool(normalize))))
+
+
+def workspace_bytes(log_n: int, batch: int, kind: int = 1) -> int:
+    out = _sz()
+    check(lib().ferrum_fft_workspace_bytes(log_n, batch, kind, ctypes.byref(out)))
+    return out.value
+
+
+def launch_count(log_n: int, batch: int, kind: int = 1) -> int:
+    out = _i()
+    check(lib().ferrum_fft_launch_count(log_n, batch, kind, ctypes.byref(out)))
+    return out.value

@@ -1,0 +1,154 @@
+/*
+ * ferrum_fft.h — C ABI of the B200 (sm_100a) FFT path.
+ *
+ * This is the drop-in boundary for the reference's FFT hot path
+ * (alejandro-soto-franco/ferrum-gpu). Every entry point takes plain pointers
+ * and sizes, returns a status code, and records a message for
+ * ferrum_last_error(). The kernels are hand-written CUDA for sm_100a; there is
+ * no CPU fallback: without a usable B200 every compute entry point returns
+ * FERRUM_ERR_CUDA.
+ *
+ * Data layout (crates/ferrum-gpu-fft/src/complex.rs:10-18): complex64
+ * interleaved [re, im] float pairs, row-major [batch][N] for 1D and
+ * [batch][N][N] for 2D. `direction` is +1 forward / -1 inverse
+ * (crates/ferrum-gpu-core/src/dim.rs:49-64). Forward is the unnormalised DFT
+ * X[k] = sum_n x[n] exp(-2 pi i n k / N); inverse is conj(FFT(conj(x))),
+ * multiplied by 1/N (1D) or 1/N^2 (2D) only when `normalize` is non-zero
+ * (crates/ferrum-gpu-fft/src/cpu.rs:106-121, cpu_2d.rs:51-63).
+ *
+ * Every `*_dev` pointer is device memory on the handle's device; `stream` is a
+ * cudaStream_t (NULL = the legacy default stream). Device-pointer calls are
+ * asynchronous with respect to the host; the host-pointer (`_host`) calls
+ * return when the result is in host memory. `in` may equal `out` (in place).
+ */
+#ifndef FERRUM_FFT_H
+#define FERRUM_FFT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int ferrum_status;
+enum {
+  FERRUM_OK = 0,
+  FERRUM_ERR_INVALID_ARG = 1,
+  FERRUM_ERR_CUDA = 2,
+  FERRUM_ERR_NCCL = 3,
+  FERRUM_ERR_TIMEOUT = 4,
+  FERRUM_ERR_ALLOC = 5,
+  FERRUM_ERR_UNSUPPORTED = 6
+};
+
+enum { FERRUM_FORWARD = 1, FERRUM_INVERSE = -1 };
+
+/* Supported sizes. 1D lengths up to 2^14 run as one HBM pass; 2^15..2^26 run
+ * the two-pass four-step. 2D images are N x N with N up to 2^14. */
+#define FERRUM_MIN_LOG_N 2
+#define FERRUM_MAX_LOG_N_SINGLE_PASS 14
+#define FERRUM_MAX_LOG_N_1D 26
+#define FERRUM_MAX_LOG_N_2D 14
+
+typedef struct ferrum_device ferrum_device;
+
+/* Library version string ("0.3.0-b200"); replaces `version()`
+ * (crates/ferrum-gpu-py/src/lib.rs:419-423). */
+const char *ferrum_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char *ferrum_last_error(void);
+
+/* Open CUDA device `ordinal`, upload every twiddle table and return a handle.
+ * Replaces `Device::new(ordinal)` (crates/ferrum-gpu-py/src/lib.rs:398-408,
+ * crates/ferrum-gpu/src/lib.rs:143-150). Thread-safe. */
+ferrum_status ferrum_device_create(int ordinal, ferrum_device **out);
+ferrum_status ferrum_device_destroy(ferrum_device *dev);
+/* Wait for all work on the device (crates/ferrum-gpu-py/src/lib.rs:410-416). */
+ferrum_status ferrum_device_sync(ferrum_device *dev);
+/* Ordinal of the device behind the handle. */
+ferrum_status ferrum_device_ordinal(const ferrum_device *dev, int *ordinal);
+
+/* Batched 1D C2C on device memory: `batch` transforms of N = 2^log_n.
+ * Device-resident form of `fft_1d_c2c_pow2` / `run_fft_flat_with_device`
+ * (crates/ferrum-gpu-py/src/lib.rs:445-504, :86-250); log_n in [2, 26].
+ * Lengths above 2^14 need a workspace of N*batch*8 bytes, taken from the
+ * device's stream-ordered memory pool. */
+ferrum_status ferrum_fft_1d_c2c_pow2(ferrum_device *dev, const void *in_dev, void *out_dev,
+                                     int log_n, size_t batch, int direction, int normalize,
+                                     void *stream);
+
+/* Same, with a caller-owned workspace of at least
+ * ferrum_fft_workspace_bytes(log_n, batch, 1) bytes (may be NULL when that is 0). */
+ferrum_status ferrum_fft_1d_c2c_pow2_ws(ferrum_device *dev, const void *in_dev, void *out_dev,
+                                        int log_n, size_t batch, int direction, int normalize,
+                                        void *workspace_dev, size_t workspace_bytes,
+                                        void *stream);
+
+/* Batched 2D C2C on device memory: `batch` images of N x N, N = 2^log_n,
+ * log_n in [2, 14]. Replaces `fft_2d_c2c_pow2` / `run_fft_2d_flat`
+ * (crates/ferrum-gpu-py/src/lib.rs:527-588, :273-375); the reference's 2D takes
+ * one image and log_n in [4, 12]. Two HBM passes: row FFTs, then column FFTs
+ * in place. */
+ferrum_status ferrum_fft_2d_c2c_pow2(ferrum_device *dev, const void *in_dev, void *out_dev,
+                                     int log_n, size_t batch, int direction, int normalize,
+                                     void *stream);
+
+/* Host-memory forms: copy in, transform, copy out, return when done. Inputs
+ * are processed in chunks so that copies overlap the kernels; pinned host
+ * buffers give full PCIe bandwidth. These are the entry points behind the
+ * Python `fft_1d_c2c_pow2` / `fft_2d_c2c_pow2` (lib.rs:445-588). */
+ferrum_status ferrum_fft_1d_c2c_pow2_host(ferrum_device *dev, const void *in_host,
+                                          void *out_host, int log_n, size_t batch,
+                                          int direction, int normalize);
+ferrum_status ferrum_fft_2d_c2c_pow2_host(ferrum_device *dev, const void *in_host,
+                                          void *out_host, int log_n, size_t batch,
+                                          int direction, int normalize);
+
+/* Workspace bytes a call needs: kind 1 = 1D, kind 2 = 2D. */
+ferrum_status ferrum_fft_workspace_bytes(int log_n, size_t batch, int kind, size_t *bytes);
+
+/* Number of kernel launches one device-pointer call makes (kind 1 = 1D,
+ * kind 2 = 2D): 1 for single-pass 1D, 2 for four-step 1D and for 2D. */
+ferrum_status ferrum_fft_launch_count(int log_n, size_t batch, int kind, int *launches);
+
+/* ---------------------------------------------------------------------------
+ * Distributed 2D (one process per GPU, NCCL over NVLink). New in this build:
+ * the reference is single-GPU. A single N x N image is split into row slabs
+ * of N/P rows; each rank holds its slab row-major. Row FFTs run locally, an
+ * NCCL all-to-all moves (N/P) x (N/P) blocks, column FFTs run on the
+ * received column slab, and a second all-to-all returns row slabs.
+ */
+typedef struct ferrum_dist_ctx ferrum_dist_ctx;
+
+/* Bytes of the opaque id rank 0 creates and every rank passes to init. */
+#define FERRUM_DIST_ID_BYTES 128
+ferrum_status ferrum_dist_get_unique_id(unsigned char id_out[FERRUM_DIST_ID_BYTES]);
+/* Collective: every rank calls it with the same id. `timeout_ms` bounds
+ * communicator set-up and every later collective wait. */
+ferrum_status ferrum_dist_init(ferrum_device *dev, const unsigned char id[FERRUM_DIST_ID_BYTES],
+                               int nranks, int rank, int timeout_ms, ferrum_dist_ctx **out);
+ferrum_status ferrum_dist_destroy(ferrum_dist_ctx *ctx);
+ferrum_status ferrum_dist_world(const ferrum_dist_ctx *ctx, int *nranks, int *rank);
+/* Workspace bytes per rank for an N x N distributed transform. */
+ferrum_status ferrum_dist_workspace_bytes(const ferrum_dist_ctx *ctx, int log_n, size_t *bytes);
+/* Collective: in/out are this rank's (N/P) x N row slab (row-major, device
+ * memory, 16-byte aligned; in == out allowed). Every rank calls it with the
+ * same arguments, on a stream of its own device. Enqueues and returns; the
+ * workspace (ferrum_dist_workspace_bytes) comes from the device's pool. */
+ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx *ctx, const void *in_slab_dev,
+                                          void *out_slab_dev, int log_n, int direction,
+                                          int normalize, void *stream);
+/* Waits for `stream` with the context's timeout. On timeout or an NCCL error
+ * the communicator is aborted and the context becomes unusable. */
+ferrum_status ferrum_dist_sync(ferrum_dist_ctx *ctx, void *stream);
+/* FERRUM_OK when (log_n, nranks) is a supported distributed shape: nranks a
+ * power of two, log_n in [4, 14], N / nranks >= 2. */
+ferrum_status ferrum_dist_check(int log_n, int nranks);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FERRUM_FFT_H */

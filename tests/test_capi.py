@@ -1,0 +1,89 @@
+"""The C ABI library loads and exports every symbol include/ferrum_fft.h
+declares; argument validation works without a GPU, and compute entry points
+fail loudly (no CPU fallback) when no B200 is present."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO, gpu_available
+
+HEADER = os.path.join(REPO, "include", "ferrum_fft.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(ferrum_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def capi():
+    from ferrum_gpu import capi as c
+
+    c.lib()
+    return c
+
+
+def test_header_and_binding_agree(capi):
+    assert declared_symbols() == sorted(capi.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(capi):
+    lib = ctypes.CDLL(capi.LIB_PATH)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert missing == []
+
+
+def test_version(capi):
+    import ferrum_gpu
+
+    assert capi.version() == "0.3.0-b200"
+    assert ferrum_gpu.version() == capi.version()
+
+
+def test_workspace_and_launch_counts(capi):
+    assert capi.workspace_bytes(12, 65536, 1) == 0
+    assert capi.workspace_bytes(20, 64, 1) == (1 << 20) * 64 * 8
+    assert capi.workspace_bytes(24, 4, 1) == (1 << 24) * 4 * 8
+    assert capi.workspace_bytes(12, 16, 2) == 0
+    assert capi.launch_count(10, 256, 1) == 1
+    assert capi.launch_count(14, 1, 1) == 1
+    assert capi.launch_count(15, 1, 1) == 2
+    assert capi.launch_count(12, 16, 2) == 2
+
+
+@pytest.mark.parametrize("log_n,batch,kind", [(1, 1, 1), (27, 1, 1), (10, 0, 1), (15, 1, 2),
+                                              (10, 1, 3)])
+def test_invalid_sizes_rejected(capi, log_n, batch, kind):
+    with pytest.raises(capi.FerrumError) as e:
+        capi.workspace_bytes(log_n, batch, kind)
+    assert e.value.status == capi.FERRUM_ERR_INVALID_ARG
+
+
+def test_null_device_rejected(capi):
+    lib = capi.lib()
+    st = lib.ferrum_fft_1d_c2c_pow2(None, 16, 16, 10, 1, 1, 0, None)
+    assert st == capi.FERRUM_ERR_INVALID_ARG
+    assert "device handle" in capi.last_error()
+    st = lib.ferrum_fft_2d_c2c_pow2_host(None, 16, 16, 10, 1, 1, 0)
+    assert st == capi.FERRUM_ERR_INVALID_ARG
+
+
+def test_dist_shape_check(capi):
+    lib = capi.lib()
+    assert lib.ferrum_dist_check(14, 8) == capi.FERRUM_OK
+    assert lib.ferrum_dist_check(14, 3) == capi.FERRUM_ERR_INVALID_ARG
+    assert lib.ferrum_dist_check(3, 2) == capi.FERRUM_ERR_INVALID_ARG
+    assert lib.ferrum_dist_check(4, 16) == capi.FERRUM_ERR_INVALID_ARG
+
+
+@pytest.mark.skipif(gpu_available(), reason="checks the no-GPU failure mode")
+def test_no_cpu_fallback_without_gpu(capi):
+    with pytest.raises(capi.FerrumError) as e:
+        capi.DeviceHandle(0)
+    assert e.value.status in (capi.FERRUM_ERR_CUDA, capi.FERRUM_ERR_UNSUPPORTED,
+                              capi.FERRUM_ERR_INVALID_ARG)
