@@ -53,7 +53,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=700)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -213,53 +213,69 @@ def run_reference(args) -> None:
 # GPU side.
 
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,"
+    """nvidia-smi samples every 50 ms; stop() keeps the samples whose
+    timestamps fall inside [t_begin, t_end] (the timed region)."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,"
              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
+    REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.t_begin = None
+        self.t_end = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
 
+    def mark_begin(self):
+        self.t_begin = datetime.datetime.now()
+
+    def mark_end(self):
+        self.t_end = datetime.datetime.now()
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except Exception:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 10]
-        loaded = []
-        reasons = set()
-        max_mhz = None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
+        rows = []
+        for r in csv.reader(io.StringIO(out)):
+            if len(r) < 11:
+                continue
             try:
-                sm, smax, util = float(r[1]), float(r[2]), float(r[3])
+                ts = datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f")
+                rows.append((ts, float(r[2]), float(r[3]), r))
             except ValueError:
                 continue
-            max_mhz = smax
-            if util >= 50:
-                loaded.append(sm)
-                for name, v in zip(names, r[6:10]):
-                    if v.strip().lower() == "active":
-                        reasons.add(name)
-        samples = loaded or [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        return {"sm_mhz": statistics.median(samples) if samples else None,
-                "sm_max_mhz": max_mhz, "reasons": sorted(reasons),
-                "samples": len(rows), "samples_under_load": len(loaded)}
+        inside = [x for x in rows if self.t_begin and self.t_end and
+                  self.t_begin <= x[0] <= self.t_end]
+        use = inside or rows
+        reasons = set()
+        for _, _, _, r in use:
+            for name, v in zip(self.REASONS, r[7:11]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(x[1] for x in use) if use else None,
+                "sm_max_mhz": use[-1][2] if use else None,
+                "reasons": sorted(reasons),
+                "samples": len(rows), "samples_in_timed_region": len(inside),
+                "window": "timed region" if inside else "whole run (timed region shorter than "
+                                                         "one sample)"}
 
 
 def run_ours(args) -> None:
@@ -324,14 +340,16 @@ def run_ours(args) -> None:
     end = torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     sampler.start()
-    time.sleep(0.3)
+    time.sleep(0.5)
     barrier()
     torch.cuda.synchronize()
+    sampler.mark_begin()
     start.record(stream)
     for k in range(args.steps):
         step(per_launch[k])
     end.record(stream)
     torch.cuda.synchronize()
+    sampler.mark_end()
     barrier()
     clocks = sampler.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end))

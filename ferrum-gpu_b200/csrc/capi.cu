@@ -234,7 +234,13 @@ ferrum_status ferrum_device_destroy(ferrum_device* dev) {
   clear_error();
   if (dev == nullptr) return FERRUM_OK;
   DeviceGuard guard(dev->ordinal);
-  cudaDeviceSynchronize();
+  if (cudaDeviceSynchronize() == cudaErrorCudartUnloading) {
+    // Called from a static destructor after the runtime shut down: the
+    // driver has already reclaimed every resource; only free the host side.
+    dev->tables = nullptr;
+    delete dev;
+    return FERRUM_OK;
+  }
   for (int i = 0; i < ferrum_device::kHostStreams; ++i) {
     if (dev->host_streams[i]) cudaStreamDestroy(dev->host_streams[i]);
     if (dev->host_dbuf[i]) cudaFree(dev->host_dbuf[i]);

@@ -24,10 +24,10 @@ constexpr int cols_fpb(int log_n) {
                     : (kColsThreads >> (log_n - plan_log_p(log_n))));
 }
 
-// Raise the dynamic shared-memory limit once per (kernel, device).
+// Raise the dynamic shared-memory limit once per (kernel, device). `done` is
+// a per-instantiation flag word owned by the caller (one bit per device).
 template <class K>
-cudaError_t ensure_smem(K kernel, size_t bytes) {
-  static std::atomic<uint64_t> done{0};
+cudaError_t ensure_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done) {
   if (bytes <= 48 * 1024) return cudaSuccess;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -48,7 +48,8 @@ cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t n
   constexpr int FPB = rows_fpb(LOGN);
   using C = RowsCfg<LOGN, LOGP, FPB, CI, CO>;
   auto k = fft_rows_kernel<LOGN, LOGP, FPB, CI, CO>;
-  cudaError_t e = ensure_smem(k, C::SMEM_BYTES);
+  static std::atomic<uint64_t> smem_done{0};
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
   const int64_t blocks = ceil_div(nfft, FPB);
   k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, log_block);
@@ -62,7 +63,8 @@ cudaError_t cols_impl(const float2* in, float2* out, const float2* tw, const Col
   constexpr int FPB = cols_fpb(LOGN);
   using C = ColsCfg<LOGN, LOGP, FPB, CI, CO, TW>;
   auto k = fft_cols_kernel<LOGN, LOGP, FPB, CI, CO, TW>;
-  cudaError_t e = ensure_smem(k, C::SMEM_BYTES);
+  static std::atomic<uint64_t> smem_done{0};
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
   const int64_t blocks = ceil_div(a.nfft, FPB);
   k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);
@@ -76,7 +78,8 @@ cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const R
   constexpr int FPB = cols_fpb(LOGN);
   using C = RowsTCfg<LOGN, LOGP, FPB, CO>;
   auto k = fft_rows_t_kernel<LOGN, LOGP, FPB, CO>;
-  cudaError_t e = ensure_smem(k, C::SMEM_BYTES);
+  static std::atomic<uint64_t> smem_done{0};
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
   const int64_t blocks = ceil_div(a.nfft, FPB);
   k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);

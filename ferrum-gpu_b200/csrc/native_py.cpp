@@ -13,7 +13,6 @@
 #include <pybind11/pybind11.h>
 
 #include <complex>
-#include <memory>
 #include <mutex>
 #include <sstream>
 #include <string>
@@ -60,19 +59,21 @@ class Device {
 
 // device=None: the reference builds a transient context and module per call
 // (lib.rs:252-264, about 200 ms). Here one handle per process is created on
-// first use and reused; results are identical.
+// first use and reused; results are identical. The handle is never
+// destroyed: a static destructor would run after the CUDA runtime has shut
+// down at process exit, and the driver reclaims the device memory anyway.
 Device& default_device() {
   static std::once_flag once;
-  static std::unique_ptr<Device> dev;
-  static std::string error;
+  static Device* dev = nullptr;
+  static std::string* error = new std::string();
   std::call_once(once, [] {
     try {
-      dev.reset(new Device(0));
+      dev = new Device(0);
     } catch (const std::exception& e) {
-      error = e.what();
+      *error = e.what();
     }
   });
-  if (!dev) throw py::value_error(error);
+  if (!dev) throw py::value_error(*error);
   return *dev;
 }
 
