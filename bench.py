@@ -1,6 +1,6 @@
 """Benchmark of the B200 FFT path (batched 1D C2C, HBM GB/s).
 
-Workload (the north-star case): batched 1D complex64
+Workload (the sweep config at its N=4096 point): batched 1D complex64
 C2C FFT, N = 4096, batch = 65536 per GPU (2 GiB), re/im i.i.d. uniform[-1, 1)
 from a seeded generator. One step = one forward pass (x -> y) and one
 inverse pass with 1/N (y -> z) through the C ABI on device-resident buffers.
@@ -89,8 +89,8 @@ def measured_peak():
 
 def profiled_traffic():
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu
-    summary (profiles/fft_rows_kernel_4096x65536.md), if present."""
-    path = os.path.join(REPO, "profiles", "fft_rows_kernel_4096x65536.md")
+    summary (profiles/fft_rows_kernel_4096x8192_full.md), if present."""
+    path = os.path.join(REPO, "profiles", "fft_rows_kernel_4096x8192_full.md")
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_launch:"):

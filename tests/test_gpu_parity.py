@@ -178,7 +178,7 @@ def test_2d_8192_in_place(capi, dev, oracle_mod):
 
 
 def test_2d_16384_properties(capi, dev, oracle_mod):
-    """16384 x 16384 (BASELINE config 5 on one GPU): row 0 of the result is
+    """16384 x 16384 (the distributed config, here on one GPU): row 0 of the result is
     the 1D FFT of the column sums; round trip recovers the input."""
     log_n = 14
     n = 1 << log_n
@@ -226,7 +226,7 @@ def test_host_pointer_2d(capi, dev, oracle_mod):
 
 @pytest.mark.parametrize("log_n,batch", [(8, 1 << 20), (10, 1 << 18), (12, 1 << 16), (14, 1 << 14)])
 def test_config_sizes_properties(capi, dev, oracle_mod, log_n, batch):
-    """2 GiB sweep sizes: sampled-row parity, round trip,
+    """2 GiB sweep sizes (N = 256..16384): sampled-row parity, round trip,
     linearity and Parseval on the full batch."""
     n = 1 << log_n
     g = torch.Generator(device="cuda").manual_seed(log_n)
@@ -260,7 +260,7 @@ def test_config_sizes_properties(capi, dev, oracle_mod, log_n, batch):
 
 @pytest.mark.parametrize("log_n,batch", [(20, 64), (24, 4)])
 def test_large_n_config_properties(capi, dev, oracle_mod, log_n, batch):
-    """BASELINE config 3 (standard normal inputs): one transform against the
+    """Large-N sizes 2^20 x 64 and 2^24 x 4 (standard normal inputs): one transform against the
     oracle, the full batch through a round trip."""
     n = 1 << log_n
     g = torch.Generator(device="cuda").manual_seed(log_n)
@@ -278,7 +278,7 @@ def test_large_n_config_properties(capi, dev, oracle_mod, log_n, batch):
 
 
 def test_2d_config4_properties(capi, dev, oracle_mod):
-    """4096 x 4096 x 16 images; one image against the
+    """2D 4096 x 4096 x 16 images: one image against the
     oracle, all through a round trip."""
     log_n, batch = 12, 16
     n = 1 << log_n
