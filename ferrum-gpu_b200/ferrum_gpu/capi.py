@@ -41,6 +41,7 @@ SIGNATURES = {
     "ferrum_device_ordinal": (_i, [_vp, ctypes.POINTER(_i)]),
     "ferrum_fft_1d_c2c_pow2": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
     "ferrum_fft_1d_c2c_pow2_ws": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp, _sz, _vp]),
+    "ferrum_fft_1d_c2c_pow2_noalloc": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
     "ferrum_fft_2d_c2c_pow2": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
     "ferrum_fft_1d_c2c_pow2_host": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i]),
     "ferrum_fft_2d_c2c_pow2_host": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i]),
@@ -140,6 +141,14 @@ def fft_1d_ws(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: i
     check(lib().ferrum_fft_1d_c2c_pow2_ws(dev.ptr, in_ptr, out_ptr, log_n, batch,
                                           _dir(direction), int(bool(normalize)), ws_ptr,
                                           ws_bytes, stream))
+
+
+def fft_1d_noalloc(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: int,
+                   direction="forward", normalize: bool = False, stream: int = 0) -> None:
+    """Allocation-free 1D transform: lengths above 2^14 use the library's
+    static 32 MiB device scratch (N * batch <= 2^22) instead of a workspace."""
+    check(lib().ferrum_fft_1d_c2c_pow2_noalloc(dev.ptr, in_ptr, out_ptr, log_n, batch,
+                                               _dir(direction), int(bool(normalize)), stream))
 
 
 def fft_2d(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch: int,

@@ -86,6 +86,21 @@ ferrum_status ferrum_fft_1d_c2c_pow2_ws(ferrum_device *dev, const void *in_dev, 
                                         void *workspace_dev, size_t workspace_bytes,
                                         void *stream);
 
+/* Allocation-free form of ferrum_fft_1d_c2c_pow2 (no counterpart in the
+ * reference). For callers that cannot allocate device memory at call time:
+ * applications whose memory belongs to their own allocator or to a pool
+ * reserved at start-up, and latency-critical loops where an allocation may
+ * block in the driver. Lengths above 2^14 use a 32 MiB file-scope __device__
+ * scratch array instead of a workspace, so N * batch must be <= 2^22 there
+ * (larger calls return FERRUM_ERR_INVALID_ARG); every GPU that loads the
+ * library keeps that array until exit. The array is shared by all calls on a
+ * device: calls that overlap on the GPU race, and none needs it zeroed. The
+ * first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture. */
+ferrum_status ferrum_fft_1d_c2c_pow2_noalloc(ferrum_device *dev, const void *in_dev,
+                                             void *out_dev, int log_n, size_t batch,
+                                             int direction, int normalize, void *stream);
+
 /* Batched 2D C2C on device memory: `batch` images of N x N, N = 2^log_n,
  * log_n in [2, 14]. Replaces `fft_2d_c2c_pow2` / `run_fft_2d_flat`
  * (crates/ferrum-gpu-py/src/lib.rs:527-588, :273-375); the reference's 2D takes
