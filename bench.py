@@ -61,6 +61,8 @@ def parse_args():
                     help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the secondary measurements (other configs, 2D 16384^2)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="transforms per GPU (default 65536 = 2 GiB; smaller only for profiling)")
     return ap.parse_args()
@@ -278,6 +280,84 @@ class ClockSampler:
                                                          "one sample)"}
 
 
+def _time_ms(fn, stream, reps: int = 5, warm: int = 2) -> float:
+    """Mean CUDA-event time of `fn` on `stream` over `reps` calls."""
+    import torch
+
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        fn()
+    b.record(stream)
+    b.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def measure_extras(capi, dev, x, y, world, rank, barrier, max_over_ranks) -> dict:
+    """Secondary measurements on the same device buffers (2^28 complex each):
+    the other sweep sizes, the large-N four-step sizes, 2D 4096^2 x 16 and the
+    16384^2 2D transform (single GPU at N=1, distributed over NCCL at N>1).
+    GB/s count 16 B per element per pass (1 pass for N <= 2^14, 2 for the
+    four-step and 2D)."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    total = x.numel()
+    out = {}
+
+    def gbs(passes, elems, ms):
+        return round(world * passes * 16 * elems / (ms * 1e-3) / 1e9, 1)
+
+    for log_n in (8, 10, 12, 14):
+        batch = total >> log_n
+        ms = max_over_ranks(_time_ms(lambda: capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), log_n,
+                                                         batch, "forward", False, sp), stream))
+        out[f"1d_N{1 << log_n}_x{batch}_fwd"] = {"GB/s": gbs(1, total, ms), "ms": round(ms, 4)}
+    for log_n, batch in ((20, 64), (24, 4)):
+        ms = max_over_ranks(_time_ms(lambda: capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), log_n,
+                                                         batch, "forward", False, sp), stream))
+        out[f"1d_N2^{log_n}_x{batch}_fwd"] = {"GB/s": gbs(2, batch << log_n, ms), "ms": round(ms, 4)}
+    ms = max_over_ranks(_time_ms(lambda: capi.fft_2d(dev, x.data_ptr(), y.data_ptr(), 12, 16,
+                                                     "forward", False, sp), stream))
+    out["2d_4096^2_x16_fwd"] = {"GB/s": gbs(2, 16 << 24, ms), "ms": round(ms, 4)}
+
+    n = 1 << 14
+    if world == 1:
+        ms = _time_ms(lambda: capi.fft_2d(dev, x.data_ptr(), y.data_ptr(), 14, 1, "forward", False,
+                                          sp), stream)
+        capi.fft_2d(dev, y.data_ptr(), y.data_ptr(), 14, 1, "inverse", True, sp)
+        torch.cuda.synchronize()
+        err = float((y - x).abs().max() / x.abs().max())
+        out["2d_16384^2_fwd"] = {"ms": round(ms, 4), "GB/s": gbs(2, n * n, ms),
+                                 "path": "single GPU (row pass + column pass)",
+                                 "roundtrip_max_rel_err": err}
+    else:
+        from ferrum_gpu.dist import Dist2D
+
+        ctx = Dist2D(dev, timeout_ms=120000)
+        rows = n // world
+        xs = x[: rows * n]
+        ys = y[: rows * n]
+        zs = torch.empty_like(xs)
+        barrier()
+        ms = max_over_ranks(_time_ms(lambda: ctx.fft_2d(xs.data_ptr(), ys.data_ptr(), 14, "forward",
+                                                        False, sp), stream))
+        ctx.fft_2d(ys.data_ptr(), zs.data_ptr(), 14, "inverse", True, sp)
+        ctx.sync(sp)
+        err = max_over_ranks(float((zs - xs).abs().max() / xs.abs().max()))
+        barrier()
+        ctx.close()
+        out["2d_16384^2_fwd"] = {"ms": round(ms, 4),
+                                 "path": f"distributed over {world} GPUs: row slabs, NCCL all-to-all",
+                                 "roundtrip_max_rel_err": err}
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -387,6 +467,11 @@ def run_ours(args) -> None:
                "steps": args.e2e_steps,
                "path": "ferrum_fft_1d_c2c_pow2_host (C ABI), pinned host buffers, forward + inverse"}
 
+    extras = None
+    if not args.no_extras and B_ == BATCH:
+        extras = measure_extras(capi, dev, x.view(-1), y.view(-1), world, rank, barrier,
+                                max_over_ranks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_leg(args.cpu_seconds)
@@ -425,6 +510,7 @@ def run_ours(args) -> None:
             "e2e": e2e,
             "clocks": clocks,
             "gpu_launches": args.steps * launches_per_step,
+            "secondary": extras,
             "roundtrip_max_rel_err": err,
         }
         print(json.dumps(line), flush=True)

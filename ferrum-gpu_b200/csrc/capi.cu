@@ -19,6 +19,7 @@
 
 #include "fft_kernels.cuh"
 #include "fft_launch.h"
+#include "passes.h"
 #include "runtime.h"
 #include "twiddle_tables.h"
 
@@ -92,63 +93,67 @@ bool is_aligned8(const void* p) { return ((uintptr_t)p & 7u) == 0; }
 }  // namespace
 
 size_t workspace_1d_bytes(int log_n, int64_t batch) {
-  if (log_n <= kMaxSinglePassLogN) return 0;
-  return ((size_t)1 << log_n) * (size_t)batch * sizeof(float2);
+  return (size_t)plan_1d(log_n, batch, false, false).ws_elems * sizeof(float2);
+}
+
+size_t workspace_2d_bytes(int log_n, int64_t batch) {
+  return (size_t)plan_2d(log_n, batch, false, false).ws_elems * sizeof(float2);
+}
+
+ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* in, float2* out,
+                       float2* ws, cudaStream_t stream) {
+  float2* bufs[3] = {const_cast<float2*>(in), out, ws};
+  for (int i = 0; i < plan.count; ++i) {
+    const PassDesc& d = plan.p[i];
+    const float2* src = bufs[(int)d.src];
+    float2* dst = bufs[(int)d.dst];
+    const float2* stw = stage_table(dev, d.log_n);
+    cudaError_t e = cudaSuccess;
+    switch (d.kind) {
+      case PassKind::Rows:
+        e = launch_rows(d.log_n, d.conj_in, d.conj_out, src, dst, stw, d.rows_nfft, d.rows_scale,
+                        stream, d.rows_log_block, dev->err_flag);
+        break;
+      case PassKind::Pass: {
+        PassArgs a = d.pa;
+        if (a.log_m > 0) {
+          a.tw_lo = tw4_lo_table(dev, a.log_m);
+          a.tw_hi = tw4_hi_table(dev, a.log_m);
+        }
+        e = launch_pass(d.log_n, d.conj_in, d.conj_out, a.log_m > 0, src, dst, stw, a, stream);
+        break;
+      }
+      case PassKind::RowsT:
+        e = launch_rows_t(d.log_n, d.conj_out, src, dst, stw, d.ra, stream);
+        break;
+    }
+    if (e != cudaSuccess)
+      return cuda_error(e, (std::string("pass ") + std::to_string(i) + " launch").c_str());
+  }
+  return FERRUM_OK;
 }
 
 ferrum_status enqueue_1d(ferrum_device* dev, const float2* in, float2* out, int log_n,
                          int64_t batch, int direction, bool normalize, float2* ws,
                          cudaStream_t stream) {
-  const bool inv = direction < 0;
-  const float scale = (inv && normalize) ? 1.0f / (float)((int64_t)1 << log_n) : 1.0f;
-  cudaError_t e;
-  if (log_n <= kMaxSinglePassLogN) {
-    e = launch_rows(log_n, inv, inv, in, out, stage_table(dev, log_n), batch, scale, stream);
-    if (e != cudaSuccess) return cuda_error(e, "fft_rows_kernel launch");
-    return FERRUM_OK;
-  }
-  // Four-step: x as N1 rows x N2 columns; pass A = column FFTs with the
-  // W_N^(n2*k1) twiddle fused into the store, pass B = row FFTs stored
-  // transposed so that X[k1 + N1*k2] lands in natural order.
-  const int l1 = four_step_log_n1(log_n), l2 = four_step_log_n2(log_n);
-  const int64_t n = (int64_t)1 << log_n;
-  ColsArgs a{};
-  a.nfft = batch << l2;
-  a.img_stride = n;
-  a.ld = (int64_t)1 << l2;
-  a.log_cols = l2;
-  a.scale = 1.0f;
-  a.tw4_lo = tw4_lo_table(dev, log_n);
-  a.tw4_hi = tw4_hi_table(dev, log_n);
-  e = launch_cols(l1, inv, false, true, in, ws, stage_table(dev, l1), a, stream);
-  if (e != cudaSuccess) return cuda_error(e, "four-step pass A launch");
-  RowsTArgs b{};
-  b.nfft = batch << l1;
-  b.log_rows = l1;
-  b.scale = scale;
-  e = launch_rows_t(l2, inv, ws, out, stage_table(dev, l2), b, stream);
-  if (e != cudaSuccess) return cuda_error(e, "four-step pass B launch");
-  return FERRUM_OK;
+  return run_plan(dev, plan_1d(log_n, batch, direction < 0, normalize), in, out, ws, stream);
 }
 
 ferrum_status enqueue_2d(ferrum_device* dev, const float2* in, float2* out, int log_n,
-                         int64_t batch, int direction, bool normalize, cudaStream_t stream) {
-  const bool inv = direction < 0;
-  const int64_t n = (int64_t)1 << log_n;
-  // cpu_2d.rs:56-62: one 1/(n*n) scale computed in float.
-  const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
-  const float2* tw = stage_table(dev, log_n);
-  cudaError_t e = launch_rows(log_n, inv, false, in, out, tw, batch * n, 1.0f, stream);
-  if (e != cudaSuccess) return cuda_error(e, "2D row pass launch");
-  ColsArgs a{};
-  a.nfft = batch * n;
-  a.img_stride = n * n;
-  a.ld = n;
-  a.log_cols = log_n;
-  a.scale = scale;
-  e = launch_cols(log_n, false, inv, false, out, out, tw, a, stream);
-  if (e != cudaSuccess) return cuda_error(e, "2D column pass launch");
-  return FERRUM_OK;
+                         int64_t batch, int direction, bool normalize, float2* ws,
+                         cudaStream_t stream) {
+  return run_plan(dev, plan_2d(log_n, batch, direction < 0, normalize), in, out, ws, stream);
+}
+
+ferrum_status check_device_flag(ferrum_device* dev) {
+  int flag = 0;
+  cudaError_t e = cudaMemcpy(&flag, dev->err_flag, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_error(e, "reading the device error flag");
+  if (flag == 0) return FERRUM_OK;
+  cudaMemset(dev->err_flag, 0, sizeof(int));
+  return set_error(FERRUM_ERR_TIMEOUT,
+                   "a kernel's bounded wait for its TMA copy expired (device flag " +
+                       std::to_string(flag) + "); its output is incomplete");
 }
 
 }  // namespace ferrum
@@ -193,7 +198,7 @@ ferrum_status ferrum_device_create(int ordinal, ferrum_device** out) {
     append_stage_tables(host, l);
     host.push_back(make_float2(1.f, 0.f));  // keeps every offset valid for 1-stage plans
   }
-  for (int l = kMaxSinglePassLogN + 1; l <= kMaxLogN; ++l) {
+  for (int l = 1; l <= kMaxLogN; ++l) {
     std::vector<float2> lo, hi;
     append_four_step_tables(lo, hi, l);
     dev->tw4_lo_off[l] = (int64_t)host.size();
@@ -212,6 +217,14 @@ ferrum_status ferrum_device_create(int ordinal, ferrum_device** out) {
     cudaFree(dev->tables);
     delete dev;
     return cuda_error(e, "cudaMemcpy(twiddle tables)");
+  }
+  e = cudaMalloc(&dev->err_flag, 256);
+  if (e == cudaSuccess) e = cudaMemset(dev->err_flag, 0, 256);
+  if (e != cudaSuccess) {
+    cudaFree(dev->tables);
+    if (dev->err_flag) cudaFree(dev->err_flag);
+    delete dev;
+    return cuda_error(e, "cudaMalloc(error flag)");
   }
   cudaMemPoolProps props = {};
   props.allocType = cudaMemAllocationTypePinned;
@@ -249,6 +262,7 @@ ferrum_status ferrum_device_destroy(ferrum_device* dev) {
     if (dev->host_pin_out[i]) cudaFreeHost(dev->host_pin_out[i]);
   }
   if (dev->pool) cudaMemPoolDestroy(dev->pool);
+  if (dev->err_flag) cudaFree(dev->err_flag);
   if (dev->tables) cudaFree(dev->tables);
   dev->tables = nullptr;
   delete dev;
@@ -261,7 +275,7 @@ ferrum_status ferrum_device_sync(ferrum_device* dev) {
   DeviceGuard guard(dev->ordinal);
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_error(e, "cudaDeviceSynchronize");
-  return FERRUM_OK;
+  return check_device_flag(dev);
 }
 
 ferrum_status ferrum_device_ordinal(const ferrum_device* dev, int* ordinal) {
@@ -283,7 +297,7 @@ ferrum_status ferrum_fft_workspace_bytes(int log_n, size_t batch, int kind, size
   if (kind == 2) {
     if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "workspace"))
       return s;
-    *bytes = 0;
+    *bytes = workspace_2d_bytes(log_n, (int64_t)batch);
     return FERRUM_OK;
   }
   return set_error(FERRUM_ERR_INVALID_ARG, "kind must be 1 (1D) or 2 (2D)");
@@ -294,13 +308,13 @@ ferrum_status ferrum_fft_launch_count(int log_n, size_t batch, int kind, int* la
   if (launches == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, "launches is NULL");
   if (kind == 1) {
     if (ferrum_status s = check_common(log_n, 2, kMaxLogN, batch, 1, "launch_count")) return s;
-    *launches = log_n <= kMaxSinglePassLogN ? 1 : 2;
+    *launches = plan_1d(log_n, (int64_t)batch, false, false).count;
     return FERRUM_OK;
   }
   if (kind == 2) {
     if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "launch_count"))
       return s;
-    *launches = 2;
+    *launches = plan_2d(log_n, (int64_t)batch, false, false).count;
     return FERRUM_OK;
   }
   return set_error(FERRUM_ERR_INVALID_ARG, "kind must be 1 (1D) or 2 (2D)");
@@ -367,8 +381,20 @@ ferrum_status ferrum_fft_2d_c2c_pow2(ferrum_device* dev, const void* in_dev, voi
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2: in/out must be 8-byte aligned");
   DeviceGuard guard(dev->ordinal);
   if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
-  return enqueue_2d(dev, (const float2*)in_dev, (float2*)out_dev, log_n, (int64_t)batch,
-                    direction, normalize != 0, (cudaStream_t)stream);
+  const size_t need = workspace_2d_bytes(log_n, (int64_t)batch);
+  void* ws = nullptr;
+  if (need > 0) {
+    cudaError_t e = cudaMallocFromPoolAsync(&ws, need, dev->pool, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMallocFromPoolAsync(2D workspace)");
+  }
+  ferrum_status s = enqueue_2d(dev, (const float2*)in_dev, (float2*)out_dev, log_n,
+                               (int64_t)batch, direction, normalize != 0, (float2*)ws,
+                               (cudaStream_t)stream);
+  if (ws) {
+    cudaError_t e = cudaFreeAsync(ws, (cudaStream_t)stream);
+    if (s == FERRUM_OK && e != cudaSuccess) return cuda_error(e, "cudaFreeAsync(2D workspace)");
+  }
+  return s;
 }
 
 }  // extern "C"

@@ -7,7 +7,8 @@
 //      destination rank, contiguously ([q][row][col]);
 //   2. NCCL all-to-all: block q goes to rank q. The received blocks, stacked
 //      by source rank, are exactly this rank's N x B column slab, row-major;
-//   3. column FFTs in place on the column slab (length N, stride B);
+//   3. column FFTs of the column slab (length N, row pitch B), one pass or,
+//      for N >= 2048, two sub-passes with 16 columns per CTA;
 //   4. NCCL all-to-all of the B x B row blocks of the column slab;
 //   5. a block gather turns the received [src][row][col] blocks back into the
 //      row-major B x N output slab.
@@ -27,6 +28,7 @@
 
 #include "fft_kernels.cuh"
 #include "fft_launch.h"
+#include "passes.h"
 #include "runtime.h"
 
 struct ferrum_dist_ctx {
@@ -253,7 +255,8 @@ ferrum_status ferrum_dist_workspace_bytes(const ferrum_dist_ctx* ctx, int log_n,
     return set_error(FERRUM_ERR_INVALID_ARG, "dist_workspace_bytes: NULL argument");
   if (ferrum_status s = ferrum_dist_check(log_n, ctx->nranks)) return s;
   const int64_t n = (int64_t)1 << log_n;
-  *bytes = ctx->nranks == 1 ? 0 : (size_t)(2 * (n / ctx->nranks) * n) * sizeof(float2);
+  *bytes = ctx->nranks == 1 ? workspace_2d_bytes(log_n, 1)
+                            : (size_t)(2 * (n / ctx->nranks) * n) * sizeof(float2);
   return FERRUM_OK;
 }
 
@@ -273,9 +276,18 @@ ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx* ctx, const void* in_s
   ferrum_device* dev = ctx->dev;
   DeviceGuard guard(dev->ordinal);
   if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
-  if (ctx->nranks == 1)
-    return enqueue_2d(dev, (const float2*)in_slab_dev, (float2*)out_slab_dev, log_n, 1, direction,
-                      normalize != 0, stream);
+  if (ctx->nranks == 1) {
+    const size_t need = workspace_2d_bytes(log_n, 1);
+    void* ws1 = nullptr;
+    if (need > 0) {
+      cudaError_t e = cudaMallocFromPoolAsync(&ws1, need, dev->pool, stream);
+      if (e != cudaSuccess) return cuda_error(e, "cudaMallocFromPoolAsync(2D workspace)");
+    }
+    ferrum_status s1 = enqueue_2d(dev, (const float2*)in_slab_dev, (float2*)out_slab_dev, log_n, 1,
+                                  direction, normalize != 0, (float2*)ws1, stream);
+    if (ws1) cudaFreeAsync(ws1, stream);
+    return s1;
+  }
 
   const bool inv = direction < 0;
   const int64_t n = (int64_t)1 << log_n;
@@ -297,19 +309,14 @@ ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx* ctx, const void* in_s
       break;
     }
     if ((s = all_to_all(ctx, wa, wb, b * b, stream)) != FERRUM_OK) break;
-    ColsArgs a{};
-    a.nfft = b;
-    a.img_stride = n * b;
-    a.ld = b;
-    a.log_cols = lb;
-    a.scale = scale;
-    e = launch_cols(log_n, false, inv, false, wb, wb, tw, a, stream);
-    if (e != cudaSuccess) {
-      s = cuda_error(e, "distributed column pass launch");
-      break;
-    }
-    if ((s = all_to_all(ctx, wb, wa, b * b, stream)) != FERRUM_OK) break;
-    e = launch_block_gather(wa, (float2*)out_slab_dev, ctx->nranks, b, b, stream);
+    // Column FFTs of the N x B column slab (row pitch B): wb -> wa, one pass or
+    // two sub-passes (the first in place on wb).
+    PassPlan cols;
+    plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::In,
+                 PassBuf::Out);
+    if ((s = run_plan(dev, cols, wb, wa, nullptr, stream)) != FERRUM_OK) break;
+    if ((s = all_to_all(ctx, wa, wb, b * b, stream)) != FERRUM_OK) break;
+    e = launch_block_gather(wb, (float2*)out_slab_dev, ctx->nranks, b, b, stream);
     if (e != cudaSuccess) {
       s = cuda_error(e, "distributed block gather launch");
       break;

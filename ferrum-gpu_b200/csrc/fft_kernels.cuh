@@ -4,11 +4,12 @@
 //
 //   fft_rows_kernel    FPB contiguous length-N transforms per CTA
 //                      (batched 1D, the 2D row pass, the distributed row pass)
-//   fft_cols_kernel    FPB adjacent columns per CTA, elements `ld` apart
-//                      (2D column pass, four-step pass A with the
-//                      W_N^(n2*k1) twiddle fused into the store)
+//   fft_pass_kernel    FPB adjacent columns per CTA, strided elements, an
+//                      optional twiddle fused into the store (2D column
+//                      passes, column passes of the multi-pass 1D transform)
 //   fft_rows_t_kernel  FPB contiguous rows per CTA, stored transposed through
-//                      shared memory (four-step pass B: X[k1 + N1*k2])
+//                      shared memory (last pass of the multi-pass 1D
+//                      transform: X[k1 + N1*k2 + ...] in natural order)
 //
 // Inverse transforms use the reference's conjugation identity
 // IFFT(x) = conj(FFT(conj(x))) (crates/ferrum-gpu-fft/src/cpu.rs:106-121),
@@ -50,9 +51,11 @@ __device__ __forceinline__ float2 epilogue(float2 v, float scale) {
   return v;
 }
 
+// Resident CTAs per SM to target: 1024 threads' worth (64 registers per
+// thread), at most 32 CTAs.
 template <int THREADS>
 struct MinBlocks {
-  static constexpr int value = (THREADS >= 1024) ? 1 : (1024 / THREADS);
+  static constexpr int value = (THREADS >= 1024) ? 1 : (1024 / THREADS > 32 ? 32 : 1024 / THREADS);
 };
 
 // ----------------------------------------------------------------------------
@@ -112,63 +115,96 @@ fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, in
 }
 
 // ----------------------------------------------------------------------------
-// Strided columns. Transform f = img * cols + col has element e at
-// in[img * img_stride + col + e * ld]. Lanes run over the FPB adjacent
-// columns first so each row segment of FPB values is one coalesced access.
-struct ColsArgs {
-  int64_t nfft;        // images * cols
-  int64_t img_stride;  // elements between images
-  int64_t ld;          // elements between consecutive elements of a column
-  int log_cols;        // log2(columns per image)
+// Strided pass. `nfft` length-N transforms, transform f = (o, j, c) with c the
+// fastest index (c < 2^log_w, j < 2^log_j): element e is read at
+//   in [o*in_o  + j*in_j  + c + e*in_e]
+// and output k is written to
+//   out[o*out_o + j*out_j + c + k*out_e],
+// multiplied, when log_m > 0, by the twiddle W_M^((c*j*tcj + (c*tc + j*tj)*k) mod M),
+// M = 2^log_m. Adjacent columns c are adjacent in memory on both sides, so a
+// CTA of FPB columns reads and writes FPB*8-byte row segments; lanes run over
+// the columns first. Used for 2D column passes (one or two sub-passes), the
+// column passes of the multi-pass 1D transform and the distributed column
+// pass.
+struct PassArgs {
+  int64_t nfft;
+  int log_w;
+  int log_j;
+  int64_t in_o, in_j, in_e;
+  int64_t out_o, out_j, out_e;
+  uint32_t tcj, tc, tj;
+  int log_m;
+  const float2* tw_lo;
+  const float2* tw_hi;
   float scale;
-  const float2* tw4_lo;  // four-step twiddle W_Ntot^e, e in [0, 4096)
-  const float2* tw4_hi;  // four-step twiddle W_Ntot^(4096 h)
 };
 
-template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW4>
-struct ColsCfg {
+FERRUM_HD __forceinline__ void pass_index(int64_t f, int log_w, int log_j, int64_t& o, int64_t& j,
+                                          int64_t& c) {
+  c = f & (((int64_t)1 << log_w) - 1);
+  j = (f >> log_w) & (((int64_t)1 << log_j) - 1);
+  o = f >> (log_w + log_j);
+}
+
+// Twiddle exponent of output k (mod 2^32; the caller masks to M).
+FERRUM_HD __forceinline__ uint32_t pass_tw_base(uint32_t c, uint32_t j, uint32_t tcj) {
+  return c * j * tcj;
+}
+FERRUM_HD __forceinline__ uint32_t pass_tw_step(uint32_t c, uint32_t j, uint32_t tc, uint32_t tj) {
+  return c * tc + j * tj;
+}
+
+template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW>
+struct PassCfg {
   using G = Geom<LOGN, LOGP>;
   static constexpr int THREADS = FPB * G::T;
   static constexpr int RS = RegionStride<LOGN, (FPB < 16 ? FPB : 16)>::value;
-  static constexpr size_t SMEM_BYTES = (size_t)FPB * RS * sizeof(float2);
+  static constexpr size_t SMEM_BYTES = G::STAGES > 1 ? (size_t)FPB * RS * sizeof(float2) : 0;
 };
 
-template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW4>
-__global__ void __launch_bounds__(ColsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW4>::THREADS,
-                                  MinBlocks<ColsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW4>::THREADS>::value)
-fft_cols_kernel(const float2* in, float2* out, const float2* __restrict__ tw, ColsArgs a) {
+template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW>
+__global__ void __launch_bounds__(PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS,
+                                  MinBlocks<PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS>::value)
+fft_pass_kernel(const float2* in, float2* out, const float2* __restrict__ tw, PassArgs a) {
   using G = Geom<LOGN, LOGP>;
-  using C = ColsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW4>;
+  using C = PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>;
   extern __shared__ float2 smem[];
-  const int c = threadIdx.x % FPB;
+  const int cl = threadIdx.x % FPB;
   const int t = threadIdx.x / FPB;
-  const int64_t f = (int64_t)blockIdx.x * FPB + c;
+  const int64_t f = (int64_t)blockIdx.x * FPB + cl;
   const bool valid = f < a.nfft;
-  const int64_t img = f >> a.log_cols;
-  const int64_t col = f & (((int64_t)1 << a.log_cols) - 1);
-  const int64_t base = img * a.img_stride + col;
+  int64_t o, j, c;
+  pass_index(f, a.log_w, a.log_j, o, j, c);
 
   float2 v[G::P];
   if (valid) {
-    const float2* src = in + base + (int64_t)t * a.ld;
-    const int64_t step = (int64_t)G::T * a.ld;
+    const float2* src = in + o * a.in_o + j * a.in_j + c + (int64_t)t * a.in_e;
+    const int64_t step = (int64_t)G::T * a.in_e;
 #pragma unroll
     for (int m = 0; m < G::P; ++m) v[m] = conj_if(ld_stream(src + step * m), CONJ_IN);
   } else {
 #pragma unroll
     for (int m = 0; m < G::P; ++m) v[m] = make_float2(0.f, 0.f);
   }
-  run_stages<LOGN, LOGP, 0>(v, smem + c * C::RS, t, tw, SyncBlock{});
+  if constexpr (FPB == 1 && G::T <= 32)
+    run_stages<LOGN, LOGP, 0>(v, smem + (C::SMEM_BYTES ? cl * C::RS : 0), t, tw, SyncWarp{});
+  else
+    run_stages<LOGN, LOGP, 0>(v, smem + (C::SMEM_BYTES ? cl * C::RS : 0), t, tw, SyncBlock{});
   if (valid) {
-    float2* dst = out + base + (int64_t)t * a.ld;
-    const int64_t step = (int64_t)G::T * a.ld;
+    float2* dst = out + o * a.out_o + j * a.out_j + c + (int64_t)t * a.out_e;
+    const int64_t step = (int64_t)G::T * a.out_e;
+    uint32_t tb = 0, ts = 0, mask = 0;
+    if constexpr (TW) {
+      tb = pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj);
+      ts = pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj);
+      mask = (1u << a.log_m) - 1u;
+    }
 #pragma unroll
     for (int m = 0; m < G::P; ++m) {
       float2 r = v[m];
-      if constexpr (TW4) {
-        // Output k1 = t + T*m of column n2 = col: multiply by W_Ntot^(n2*k1).
-        const uint32_t e = (uint32_t)col * (uint32_t)(t + G::T * m);
-        r = c_mul(r, four_step_twiddle(a.tw4_lo, a.tw4_hi, e));
+      if constexpr (TW) {
+        const uint32_t e = (tb + ts * (uint32_t)(t + G::T * m)) & mask;
+        r = c_mul(r, four_step_twiddle(a.tw_lo, a.tw_hi, e));
       }
       st_stream(dst + step * m, epilogue<CONJ_OUT>(r, a.scale));
     }
@@ -176,11 +212,18 @@ fft_cols_kernel(const float2* in, float2* out, const float2* __restrict__ tw, Co
 }
 
 // ----------------------------------------------------------------------------
-// Rows stored transposed. Transform b holds `rows` contiguous rows of length N;
-// output element k2 of row k1 goes to out[b * rows * N + k1 + rows * k2].
+// Rows stored transposed. Transform f = (o, j, c), c fastest: its N elements
+// are contiguous at in[o*in_o + j*in_j + c*in_c], and output k goes to
+// out[o*out_o + j*out_j + c + k*out_e]. FPB adjacent c share a CTA, which
+// transposes them through shared memory so that stores run over c
+// (FPB*8-byte segments). Used for the last pass of the multi-pass 1D
+// transform, where X[k1 + N1*k2 + ...] must land in natural order.
 struct RowsTArgs {
-  int64_t nfft;  // transforms * rows
-  int log_rows;  // log2(rows per transform)
+  int64_t nfft;
+  int log_w;
+  int log_j;
+  int64_t in_o, in_j, in_c;
+  int64_t out_o, out_j, out_e;
   float scale;
 };
 
@@ -206,7 +249,9 @@ fft_rows_t_kernel(const float2* in, float2* out, const float2* __restrict__ tw, 
 
   float2 v[G::P];
   if (valid) {
-    const float2* src = in + f * G::N + t;
+    int64_t o, j, c;
+    pass_index(f, a.log_w, a.log_j, o, j, c);
+    const float2* src = in + o * a.in_o + j * a.in_j + c * a.in_c + t;
 #pragma unroll
     for (int m = 0; m < G::P; ++m) v[m] = ld_stream(src + G::T * m);
   } else {
@@ -228,15 +273,14 @@ fft_rows_t_kernel(const float2* in, float2* out, const float2* __restrict__ tw, 
   const int e0 = threadIdx.x / FPB;
   const int64_t f2 = (int64_t)blockIdx.x * FPB + g2;
   if (f2 < a.nfft) {
-    const int64_t rows = (int64_t)1 << a.log_rows;
-    const int64_t img = f2 >> a.log_rows;
-    const int64_t k1 = f2 & (rows - 1);
-    float2* dst = out + img * rows * G::N + k1;
+    int64_t o, j, c;
+    pass_index(f2, a.log_w, a.log_j, o, j, c);
+    float2* dst = out + o * a.out_o + j * a.out_j + c;
     const float2* row = smem + g2 * C::RS;
 #pragma unroll
     for (int q = 0; q < G::P; ++q) {
       const int e = e0 + G::T * q;
-      st_stream(dst + rows * e, epilogue<CONJ_OUT>(row[smem_pad(e)], a.scale));
+      st_stream(dst + a.out_e * e, epilogue<CONJ_OUT>(row[smem_pad(e)], a.scale));
     }
   }
 }

@@ -3,11 +3,18 @@
 
 #include "fft_kernels.cuh"
 #include "fft_launch.h"
+#include "fft_rows_tma.cuh"
 
 namespace ferrum {
 namespace {
 
 constexpr int kRowsThreads = 256;   // batched rows: 256 threads per CTA up to N = 4096
+// The persistent TMA-prefetch rows kernel (fft_rows_tma.cuh) measured slower
+// than fft_rows_kernel on B200 for every N in 32..4096 at 2 GiB (4.87 vs 5.36
+// TB/s at N = 4096): the staging copy adds a shared-memory write and read per
+// element and costs one resident CTA per SM, and the kernel is bound by the
+// L1/shared pipe and issue rate rather than by DRAM latency. It stays off.
+constexpr bool kRowsTmaEnabled = false;
 constexpr int kColsThreads = 512;   // strided passes: up to 16 columns / rows per CTA
 
 constexpr int rows_fpb(int log_n) {
@@ -56,13 +63,45 @@ cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t n
   return cudaGetLastError();
 }
 
+// Persistent TMA-prefetch variant (fft_rows_tma.cuh): one CTA per resident
+// slot, every CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+template <int LOGN, bool CI, bool CO>
+cudaError_t rows_tma_impl(const float2* in, float2* out, const float2* tw, int64_t nfft,
+                          float scale, int* err, cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = rows_fpb(LOGN);
+  using C = RowsTmaCfg<LOGN, LOGP, FPB, CI, CO>;
+  auto k = fft_rows_tma_kernel<LOGN, LOGP, FPB, CI, CO>;
+  static std::atomic<uint64_t> smem_done{0};
+  static std::atomic<int> grid_cache[64];
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
+  if (e != cudaSuccess) return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  int resident = grid_cache[dev & 63].load(std::memory_order_relaxed);
+  if (resident == 0) {
+    int per_sm = 0, sms = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, C::THREADS, C::SMEM_BYTES)) !=
+        cudaSuccess)
+      return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return e;
+    resident = (per_sm < 1 ? 1 : per_sm) * sms;
+    grid_cache[dev & 63].store(resident, std::memory_order_relaxed);
+  }
+  const int64_t tiles = ceil_div(nfft, FPB);
+  const int64_t grid = tiles < resident ? tiles : resident;
+  k<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, err);
+  return cudaGetLastError();
+}
+
 template <int LOGN, bool CI, bool CO, bool TW>
-cudaError_t cols_impl(const float2* in, float2* out, const float2* tw, const ColsArgs& a,
+cudaError_t pass_impl(const float2* in, float2* out, const float2* tw, const PassArgs& a,
                       cudaStream_t s) {
   constexpr int LOGP = plan_log_p(LOGN);
   constexpr int FPB = cols_fpb(LOGN);
-  using C = ColsCfg<LOGN, LOGP, FPB, CI, CO, TW>;
-  auto k = fft_cols_kernel<LOGN, LOGP, FPB, CI, CO, TW>;
+  using C = PassCfg<LOGN, LOGP, FPB, CI, CO, TW>;
+  auto k = fft_pass_kernel<LOGN, LOGP, FPB, CI, CO, TW>;
   static std::atomic<uint64_t> smem_done{0};
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
@@ -88,7 +127,17 @@ cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const R
 
 template <int LOGN>
 cudaError_t rows_dispatch(bool ci, bool co, const float2* in, float2* out, const float2* tw,
-                          int64_t nfft, float scale, int lb, cudaStream_t s) {
+                          int64_t nfft, float scale, int lb, int* err, cudaStream_t s) {
+  if constexpr (kRowsTmaEnabled && LOGN >= 4 && LOGN <= 12) {
+    // TMA bulk copies need a 16-byte aligned source; blocked stores keep the
+    // plain kernel.
+    if (err != nullptr && lb >= LOGN && ((uintptr_t)in & 15u) == 0) {
+      if (ci && co) return rows_tma_impl<LOGN, true, true>(in, out, tw, nfft, scale, err, s);
+      if (ci) return rows_tma_impl<LOGN, true, false>(in, out, tw, nfft, scale, err, s);
+      if (co) return rows_tma_impl<LOGN, false, true>(in, out, tw, nfft, scale, err, s);
+      return rows_tma_impl<LOGN, false, false>(in, out, tw, nfft, scale, err, s);
+    }
+  }
   if (ci && co) return rows_impl<LOGN, true, true>(in, out, tw, nfft, scale, lb, s);
   if (ci) return rows_impl<LOGN, true, false>(in, out, tw, nfft, scale, lb, s);
   if (co) return rows_impl<LOGN, false, true>(in, out, tw, nfft, scale, lb, s);
@@ -96,21 +145,17 @@ cudaError_t rows_dispatch(bool ci, bool co, const float2* in, float2* out, const
 }
 
 template <int LOGN>
-cudaError_t cols_dispatch(bool ci, bool co, bool tw4, const float2* in, float2* out,
-                          const float2* tw, const ColsArgs& a, cudaStream_t s) {
-  if (tw4) {
-    if constexpr (LOGN >= 7 && LOGN <= 13) {
-      if (co) return cudaErrorInvalidValue;  // four-step pass A never conjugates its output
-      if (ci) return cols_impl<LOGN, true, false, true>(in, out, tw, a, s);
-      return cols_impl<LOGN, false, false, true>(in, out, tw, a, s);
-    } else {
-      return cudaErrorInvalidValue;
-    }
+cudaError_t pass_dispatch(bool ci, bool co, bool tw, const float2* in, float2* out,
+                          const float2* stw, const PassArgs& a, cudaStream_t s) {
+  if (tw) {
+    if (co) return cudaErrorInvalidValue;  // a twiddled pass is never the last one
+    if (ci) return pass_impl<LOGN, true, false, true>(in, out, stw, a, s);
+    return pass_impl<LOGN, false, false, true>(in, out, stw, a, s);
   }
-  if (ci && co) return cols_impl<LOGN, true, true, false>(in, out, tw, a, s);
-  if (ci) return cols_impl<LOGN, true, false, false>(in, out, tw, a, s);
-  if (co) return cols_impl<LOGN, false, true, false>(in, out, tw, a, s);
-  return cols_impl<LOGN, false, false, false>(in, out, tw, a, s);
+  if (ci && co) return pass_impl<LOGN, true, true, false>(in, out, stw, a, s);
+  if (ci) return cudaErrorInvalidValue;
+  if (co) return pass_impl<LOGN, false, true, false>(in, out, stw, a, s);
+  return pass_impl<LOGN, false, false, false>(in, out, stw, a, s);
 }
 
 template <int LOGN>
@@ -155,12 +200,13 @@ cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, 
 
 cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
                         const float2* tw, int64_t nfft, float scale, cudaStream_t stream,
-                        int log_block) {
+                        int log_block, int* err_flag) {
   if (log_block < 0 || log_block > log_n) log_block = log_n;
   switch (log_n) {
 #define X(L) \
   case L:    \
-    return rows_dispatch<L>(conj_in, conj_out, in, out, tw, nfft, scale, log_block, stream);
+    return rows_dispatch<L>(conj_in, conj_out, in, out, tw, nfft, scale, log_block, err_flag, \
+                            stream);
     FERRUM_CASE_2_14(X)
 #undef X
     default:
@@ -168,35 +214,18 @@ cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in
   }
 }
 
-LaunchShape rows_shape(int log_n, int64_t nfft) {
-  const int lp = plan_log_p(log_n);
-  const int t = 1 << (log_n - lp);
-  const int fpb = t <= kRowsThreads ? kRowsThreads / t : 1;
-  const int stride = (1 << log_n) + ((1 << log_n) >> 4) + 16;
-  return LaunchShape{ceil_div(nfft, fpb), fpb * t,
-                     plan_num_stages(log_n, lp) > 1 ? (size_t)fpb * stride * 8 : 0};
-}
-
-cudaError_t launch_cols(int log_n, bool conj_in, bool conj_out, bool tw4, const float2* in,
-                        float2* out, const float2* tw, const ColsArgs& args, cudaStream_t stream) {
+cudaError_t launch_pass(int log_n, bool conj_in, bool conj_out, bool tw, const float2* in,
+                        float2* out, const float2* stage_tw, const PassArgs& args,
+                        cudaStream_t stream) {
   switch (log_n) {
 #define X(L) \
   case L:    \
-    return cols_dispatch<L>(conj_in, conj_out, tw4, in, out, tw, args, stream);
+    return pass_dispatch<L>(conj_in, conj_out, tw, in, out, stage_tw, args, stream);
     FERRUM_CASE_2_14(X)
 #undef X
     default:
       return cudaErrorInvalidValue;
   }
-}
-
-LaunchShape cols_shape(int log_n, int64_t nfft) {
-  const int lp = plan_log_p(log_n);
-  const int t = 1 << (log_n - lp);
-  int fpb = kColsThreads / t;
-  fpb = fpb < 1 ? 1 : (fpb > 16 ? 16 : fpb);
-  const int stride = (1 << log_n) + ((1 << log_n) >> 4) + 16;
-  return LaunchShape{ceil_div(nfft, fpb), fpb * t, (size_t)fpb * stride * 8};
 }
 
 cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* out,
@@ -205,13 +234,11 @@ cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* ou
 #define X(L) \
   case L:    \
     return rows_t_dispatch<L>(conj_out, in, out, tw, args, stream);
-    X(8) X(9) X(10) X(11) X(12) X(13)
+    X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
 #undef X
     default:
       return cudaErrorInvalidValue;
   }
 }
-
-LaunchShape rows_t_shape(int log_n, int64_t nfft) { return cols_shape(log_n, nfft); }
 
 }  // namespace ferrum

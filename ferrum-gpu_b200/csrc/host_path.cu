@@ -107,7 +107,8 @@ ferrum_status run_host(ferrum_device* dev, const void* in_host, void* out_host, 
   const size_t units_per_chunk = std::max<size_t>(1, kChunkTarget / unit_bytes);
   const size_t chunk_units = std::min(units_per_chunk, batch);
   const size_t chunk_bytes = chunk_units * unit_bytes;
-  const size_t ws_bytes = kind == 1 ? workspace_1d_bytes(log_n, (int64_t)chunk_units) : 0;
+  const size_t ws_bytes = kind == 1 ? workspace_1d_bytes(log_n, (int64_t)chunk_units)
+                                    : workspace_2d_bytes(log_n, (int64_t)chunk_units);
   const bool direct_in = is_pinned_or_device(in_host);
   const bool direct_out = is_pinned_or_device(out_host);
 
@@ -154,7 +155,8 @@ ferrum_status run_host(ferrum_device* dev, const void* in_host, void* out_host, 
       status = enqueue_1d(dev, buf, buf, log_n, (int64_t)units, direction, normalize != 0,
                           (float2*)dev->host_ws[s], st);
     else
-      status = enqueue_2d(dev, buf, buf, log_n, (int64_t)units, direction, normalize != 0, st);
+      status = enqueue_2d(dev, buf, buf, log_n, (int64_t)units, direction, normalize != 0,
+                          (float2*)dev->host_ws[s], st);
     if (status != FERRUM_OK) break;
     void* dst = direct_out ? (char*)out_host + off : dev->host_pin_out[s];
     e = cudaMemcpyAsync(dst, dev->host_dbuf[s], bytes, cudaMemcpyDefault, st);
@@ -170,6 +172,7 @@ ferrum_status run_host(ferrum_device* dev, const void* in_host, void* out_host, 
     ferrum_status fs = finish(s);
     if (status == FERRUM_OK) status = fs;
   }
+  if (status == FERRUM_OK) status = check_device_flag(dev);
   return status;
 }
 

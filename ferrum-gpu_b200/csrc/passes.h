@@ -1,0 +1,214 @@
+// Pass planner: turns a transform request into an ordered list of kernel
+// passes over HBM. Shared by the runtime (capi.cu, dist.cu) and the CPU
+// emulator in the test suite, which executes the same plans.
+//
+// Every pass reads and writes each element once, with row segments of at
+// least 64-128 bytes:
+//   * 1D, N <= 2^14: one fft_rows_kernel pass.
+//   * 1D, 2^15..2^21: two passes, N = N1*N2, x[n2 + N2*n1]:
+//       A  DFT over n1 (columns of the N1 x N2 view), times W_N^(n2*k1);
+//       B  DFT over n2 (rows), stored transposed to X[k1 + N1*k2].
+//   * 1D, 2^22..2^26: three passes, N = N1*N2*N3, x[n3 + N3*n2 + N3*N2*n1]:
+//       1  DFT over n1, times W_{N1 N2}^(n2*k1);
+//       2  DFT over n2, times W_N^(n3*(k1 + N1*k2));
+//       3  DFT over n3 (rows), stored to X[k1 + N1*k2 + N1*N2*k3].
+//   * 2D N x N, N <= 1024: row pass, then one column pass in place.
+//   * 2D, N >= 2048: columns first as two sub-passes (N = A*B, row a + A*b:
+//     DFT over b times W_N^(a*kb), then DFT over a stored to row kb + B*ka),
+//     then the row pass, which also applies the inverse's conjugate and scale.
+// The index identities are the Cooley-Tukey splits; the reference's CPU
+// Stockham (crates/ferrum-gpu-fft/src/cpu.rs) defines the results they must
+// reproduce.
+#pragma once
+
+#include <stdint.h>
+
+#include "fft_kernels.cuh"
+#include "plan.h"
+
+namespace ferrum {
+
+enum class PassKind : int { Rows = 0, Pass = 1, RowsT = 2 };
+enum class PassBuf : int { In = 0, Out = 1, Ws = 2 };
+
+struct PassDesc {
+  PassKind kind;
+  int log_n;  // transform length of the pass
+  bool conj_in, conj_out;
+  PassBuf src, dst;
+  // Rows
+  int64_t rows_nfft;
+  int rows_log_block;
+  float rows_scale;
+  // Pass / RowsT (twiddle tables are filled in by the executor from log_m)
+  PassArgs pa;
+  RowsTArgs ra;
+};
+
+struct PassPlan {
+  int count = 0;
+  PassDesc p[4];
+  int64_t ws_elems = 0;  // workspace (complex values) the plan needs
+};
+
+inline PassDesc make_rows(int log_n, int64_t nfft, bool ci, bool co, float scale, PassBuf src,
+                          PassBuf dst, int log_block = -1) {
+  PassDesc d{};
+  d.kind = PassKind::Rows;
+  d.log_n = log_n;
+  d.conj_in = ci;
+  d.conj_out = co;
+  d.src = src;
+  d.dst = dst;
+  d.rows_nfft = nfft;
+  d.rows_log_block = log_block;
+  d.rows_scale = scale;
+  return d;
+}
+
+inline PassDesc make_pass(int log_n, bool ci, bool co, PassBuf src, PassBuf dst, const PassArgs& a) {
+  PassDesc d{};
+  d.kind = PassKind::Pass;
+  d.log_n = log_n;
+  d.conj_in = ci;
+  d.conj_out = co;
+  d.src = src;
+  d.dst = dst;
+  d.pa = a;
+  return d;
+}
+
+inline PassDesc make_rows_t(int log_n, bool co, PassBuf src, PassBuf dst, const RowsTArgs& a) {
+  PassDesc d{};
+  d.kind = PassKind::RowsT;
+  d.log_n = log_n;
+  d.conj_out = co;
+  d.src = src;
+  d.dst = dst;
+  d.ra = a;
+  return d;
+}
+
+inline PassArgs pass_args(int64_t nfft, int log_w, int log_j, int64_t in_o, int64_t in_j,
+                          int64_t in_e, int64_t out_o, int64_t out_j, int64_t out_e) {
+  PassArgs a{};
+  a.nfft = nfft;
+  a.log_w = log_w;
+  a.log_j = log_j;
+  a.in_o = in_o;
+  a.in_j = in_j;
+  a.in_e = in_e;
+  a.out_o = out_o;
+  a.out_j = out_j;
+  a.out_e = out_e;
+  a.scale = 1.0f;
+  return a;
+}
+
+// Passes of a multi-pass 1D transform.
+inline int plan_1d_passes(int log_n) { return log_n <= kMaxSinglePassLogN ? 1 : (log_n <= 21 ? 2 : 3); }
+
+inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
+  PassPlan pl;
+  const int64_t n = (int64_t)1 << log_n;
+  const float scale = (inv && normalize) ? 1.0f / (float)n : 1.0f;
+  const int np = plan_1d_passes(log_n);
+  if (np == 1) {
+    pl.p[pl.count++] = make_rows(log_n, batch, inv, inv, scale, PassBuf::In, PassBuf::Out);
+    return pl;
+  }
+  pl.ws_elems = n * batch;
+  if (np == 2) {
+    const int l1 = log_n / 2, l2 = log_n - l1;
+    const int64_t n1 = (int64_t)1 << l1, n2 = (int64_t)1 << l2;
+    PassArgs a = pass_args(batch * n2, l2, 0, n, 0, n2, n, 0, n2);
+    a.tc = 1;
+    a.log_m = log_n;
+    pl.p[pl.count++] = make_pass(l1, inv, false, PassBuf::In, PassBuf::Ws, a);
+    RowsTArgs b{};
+    b.nfft = batch * n1;
+    b.log_w = l1;
+    b.log_j = 0;
+    b.in_o = n;
+    b.in_c = n2;
+    b.out_o = n;
+    b.out_e = n1;
+    b.scale = scale;
+    pl.p[pl.count++] = make_rows_t(l2, inv, PassBuf::Ws, PassBuf::Out, b);
+    return pl;
+  }
+  // Three passes: the row pass (last) gets the largest factor.
+  const int l1 = log_n / 3, l2 = (log_n - l1) / 2, l3 = log_n - l1 - l2;
+  const int64_t n1 = (int64_t)1 << l1, n2 = (int64_t)1 << l2, n3 = (int64_t)1 << l3;
+  PassArgs a1 = pass_args(batch * n2 * n3, l3, l2, n, n3, n2 * n3, n, n3, n2 * n3);
+  a1.tj = 1;
+  a1.log_m = l1 + l2;
+  pl.p[pl.count++] = make_pass(l1, inv, false, PassBuf::In, PassBuf::Ws, a1);
+  PassArgs a2 = pass_args(batch * n1 * n3, l3, l1, n, n2 * n3, n3, n, n2 * n3, n3);
+  a2.tcj = 1;
+  a2.tc = (uint32_t)n1;
+  a2.log_m = log_n;
+  pl.p[pl.count++] = make_pass(l2, false, false, PassBuf::Ws, PassBuf::Ws, a2);
+  RowsTArgs b{};
+  b.nfft = batch * n1 * n2;
+  b.log_w = l1;
+  b.log_j = l2;
+  b.in_o = n;
+  b.in_j = n3;
+  b.in_c = n2 * n3;
+  b.out_o = n;
+  b.out_j = n1;
+  b.out_e = n1 * n2;
+  b.scale = scale;
+  pl.p[pl.count++] = make_rows_t(l3, inv, PassBuf::Ws, PassBuf::Out, b);
+  return pl;
+}
+
+// Column FFTs of length 2^log_n over `width` adjacent columns (row pitch
+// `ld`), for `images` blocks `img_stride` apart, from `src` to `dst`. One pass
+// when the pass kernel covers >= 8 columns per CTA (N <= 1024), otherwise two
+// sub-passes through `mid`. The last pass applies conj_out / scale.
+inline void plan_columns(PassPlan& pl, int log_n, int log_width, int64_t ld, int64_t images,
+                         int64_t img_stride, bool ci, bool co, float scale, PassBuf src,
+                         PassBuf mid, PassBuf dst) {
+  const int64_t width = (int64_t)1 << log_width;
+  if (log_n <= 10) {
+    PassArgs a = pass_args(images * width, log_width, 0, img_stride, 0, ld, img_stride, 0, ld);
+    a.scale = scale;
+    pl.p[pl.count++] = make_pass(log_n, ci, co, src, dst, a);
+    return;
+  }
+  const int la = log_n / 2, lb = log_n - la;
+  const int64_t na = (int64_t)1 << la, nb = (int64_t)1 << lb;
+  // Sub-pass 1: DFT over b of rows a + A*b, times W_N^(a*kb), same positions.
+  PassArgs a1 = pass_args(images * width * na, log_width, la, img_stride, ld, na * ld, img_stride,
+                          ld, na * ld);
+  a1.tj = 1;
+  a1.log_m = log_n;
+  pl.p[pl.count++] = make_pass(lb, ci, false, src, mid, a1);
+  // Sub-pass 2: DFT over a of rows A*kb + a, stored to row kb + B*ka.
+  PassArgs a2 = pass_args(images * width * nb, log_width, lb, img_stride, na * ld, ld, img_stride,
+                          ld, nb * ld);
+  a2.scale = scale;
+  pl.p[pl.count++] = make_pass(la, false, co, mid, dst, a2);
+}
+
+inline PassPlan plan_2d(int log_n, int64_t batch, bool inv, bool normalize) {
+  PassPlan pl;
+  const int64_t n = (int64_t)1 << log_n;
+  // cpu_2d.rs:56-62: one 1/(n*n) scale computed in float.
+  const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
+  if (log_n <= 10) {
+    pl.p[pl.count++] = make_rows(log_n, batch * n, inv, false, 1.0f, PassBuf::In, PassBuf::Out);
+    plan_columns(pl, log_n, log_n, n, batch, n * n, false, inv, scale, PassBuf::Out, PassBuf::Out,
+                 PassBuf::Out);
+    return pl;
+  }
+  pl.ws_elems = batch * n * n;
+  plan_columns(pl, log_n, log_n, n, batch, n * n, inv, false, 1.0f, PassBuf::In, PassBuf::Out,
+               PassBuf::Ws);
+  pl.p[pl.count++] = make_rows(log_n, batch * n, false, inv, scale, PassBuf::Ws, PassBuf::Out);
+  return pl;
+}
+
+}  // namespace ferrum

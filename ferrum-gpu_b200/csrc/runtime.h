@@ -20,6 +20,7 @@ struct ferrum_device {
   int64_t tw4_lo_off[ferrum::kMaxLogN + 1] = {};
   int64_t tw4_hi_off[ferrum::kMaxLogN + 1] = {};
   cudaMemPool_t pool = nullptr;  // stream-ordered workspace pool
+  int* err_flag = nullptr;       // device word set by kernels whose bounded waits expire
 
   // Host-pointer path resources (grown on demand, guarded by host_mu).
   std::mutex host_mu;
@@ -61,8 +62,17 @@ const float2* tw4_hi_table(const ferrum_device* dev, int log_n);
 ferrum_status enqueue_1d(ferrum_device* dev, const float2* in, float2* out, int log_n,
                          int64_t batch, int direction, bool normalize, float2* ws,
                          cudaStream_t stream);
+// `ws` must hold workspace_2d_bytes(log_n, batch) bytes (may be NULL when 0).
 ferrum_status enqueue_2d(ferrum_device* dev, const float2* in, float2* out, int log_n,
-                         int64_t batch, int direction, bool normalize, cudaStream_t stream);
+                         int64_t batch, int direction, bool normalize, float2* ws,
+                         cudaStream_t stream);
 size_t workspace_1d_bytes(int log_n, int64_t batch);
+size_t workspace_2d_bytes(int log_n, int64_t batch);
+struct PassPlan;
+// Enqueue every pass of `plan`; buffer roles In/Out/Ws map to in/out/ws.
+ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* in, float2* out,
+                       float2* ws, cudaStream_t stream);
+// Reads and clears the device error flag; FERRUM_ERR_TIMEOUT if it was set.
+ferrum_status check_device_flag(ferrum_device* dev);
 
 }  // namespace ferrum

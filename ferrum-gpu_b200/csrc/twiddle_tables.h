@@ -32,13 +32,16 @@ inline void append_stage_tables(std::vector<float2>& out, int log_n) {
   }
 }
 
-// Four-step tables of a length-2^log_n transform: LO[e] = W_N^e for
-// e < 2^kFourStepLoBits, HI[h] = W_N^(h * 2^kFourStepLoBits).
-inline void append_four_step_tables(std::vector<float2>& lo, std::vector<float2>& hi, int log_n) {
-  const int64_t n = (int64_t)1 << log_n;
-  for (int64_t e = 0; e < ((int64_t)1 << kFourStepLoBits); ++e) lo.push_back(root_of_unity(e, n));
-  for (int64_t h = 0; h < (n >> kFourStepLoBits); ++h)
-    hi.push_back(root_of_unity(h << kFourStepLoBits, n));
+// Two-level twiddle tables of modulus M = 2^log_m (used by the pass kernels'
+// fused twiddle multiply): LO[e] = W_M^e for e < min(M, 2^kFourStepLoBits),
+// HI[h] = W_M^(h * 2^kFourStepLoBits) for h < max(1, M / 2^kFourStepLoBits),
+// so W_M^e = HI[e >> kFourStepLoBits] * LO[e mod 2^kFourStepLoBits].
+inline void append_four_step_tables(std::vector<float2>& lo, std::vector<float2>& hi, int log_m) {
+  const int64_t m = (int64_t)1 << log_m;
+  const int64_t lo_n = m < ((int64_t)1 << kFourStepLoBits) ? m : ((int64_t)1 << kFourStepLoBits);
+  const int64_t hi_n = m >> kFourStepLoBits ? (m >> kFourStepLoBits) : 1;
+  for (int64_t e = 0; e < lo_n; ++e) lo.push_back(root_of_unity(e, m));
+  for (int64_t h = 0; h < hi_n; ++h) hi.push_back(root_of_unity(h << kFourStepLoBits, m));
 }
 
 }  // namespace ferrum

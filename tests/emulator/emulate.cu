@@ -1,19 +1,22 @@
 // CPU emulator of the sm_100a FFT kernels — test infrastructure only.
 //
-// Runs, on the host, the exact per-thread code the kernels run: the radix
-// plans (plan.h), the twiddle tables the runtime uploads (twiddle_tables.h),
-// stage_compute / stage_out_pos / stage_slot / smem_pad (stockham.cuh), the
-// four-step twiddle lookup and the distributed blocked layout. Each thread
-// group is simulated thread by thread between barriers, and every shared
-// memory exchange is checked to be a permutation (each padded slot written
-// exactly once and read exactly once). The tests compare its output with the
-// CPU oracle, so index-arithmetic bugs show up without a GPU.
+// Executes, on the host, the same pass plans the runtime launches
+// (ferrum-gpu_b200/csrc/passes.h) with the exact per-thread code of the
+// kernels: the radix plans (plan.h), the twiddle tables the runtime uploads
+// (twiddle_tables.h), stage_compute / stage_out_pos / stage_slot / smem_pad
+// (stockham.cuh), pass_index / pass_tw_base / pass_tw_step and the two-level
+// twiddle lookup (fft_kernels.cuh), and the distributed blocked layout. Each
+// thread group is simulated thread by thread between barriers, and every
+// shared-memory exchange is checked to be a permutation (each padded slot
+// written exactly once and read exactly once). The tests compare its output
+// with the CPU oracle, so planner and index-arithmetic bugs show up without a
+// GPU.
 #include <stdint.h>
 #include <string.h>
 
 #include <vector>
 
-#include "../../ferrum-gpu_b200/csrc/stockham.cuh"
+#include "../../ferrum-gpu_b200/csrc/passes.h"
 #include "../../ferrum-gpu_b200/csrc/twiddle_tables.h"
 
 using namespace ferrum;
@@ -86,19 +89,91 @@ int run_group(int log_n, const float2* x, float2* y, const float2* tw) {
 
 struct Tables {
   std::vector<float2> stage[kMaxSinglePassLogN + 1];
-  std::vector<float2> lo, hi;
-  Tables(int log_n) {
+  std::vector<float2> lo[kMaxLogN + 1], hi[kMaxLogN + 1];
+  Tables() {
     for (int l = 2; l <= kMaxSinglePassLogN; ++l) {
       append_stage_tables(stage[l], l);
       stage[l].push_back(make_float2(1.f, 0.f));
     }
-    if (log_n > kMaxSinglePassLogN) append_four_step_tables(lo, hi, log_n);
+    for (int l = 1; l <= kMaxLogN; ++l) append_four_step_tables(lo[l], hi[l], l);
   }
 };
+
+const Tables& tables() {
+  static Tables t;
+  return t;
+}
 
 float2 conj_if(float2 v, bool c) { return c ? make_float2(v.x, -v.y) : v; }
 float2 epi(float2 v, bool conj_out, float scale) {
   return conj_out ? make_float2(v.x * scale, -v.y * scale) : v;
+}
+
+// One pass of a plan, FFT by FFT (each touches disjoint elements, so in-place
+// passes behave as on the GPU).
+int run_pass(const PassDesc& d, const float2* src, float2* dst) {
+  const Tables& tab = tables();
+  const int64_t n = (int64_t)1 << d.log_n;
+  const float2* stw = tab.stage[d.log_n].data();
+  std::vector<float2> x(n);
+  switch (d.kind) {
+    case PassKind::Rows: {
+      const int lb = (d.rows_log_block < 0 || d.rows_log_block > d.log_n) ? d.log_n
+                                                                          : d.rows_log_block;
+      for (int64_t f = 0; f < d.rows_nfft; ++f) {
+        for (int64_t e = 0; e < n; ++e) x[e] = conj_if(src[f * n + e], d.conj_in);
+        if (int rc = run_group(d.log_n, x.data(), x.data(), stw)) return rc;
+        for (int64_t e = 0; e < n; ++e) {
+          const int64_t at = lb >= d.log_n ? f * n + e : blocked_index(f, e, lb, d.rows_nfft);
+          dst[at] = epi(x[e], d.conj_out, d.rows_scale);
+        }
+      }
+      return 0;
+    }
+    case PassKind::Pass: {
+      const PassArgs& a = d.pa;
+      const uint32_t mask = a.log_m > 0 ? (1u << a.log_m) - 1u : 0u;
+      for (int64_t f = 0; f < a.nfft; ++f) {
+        int64_t o, j, c;
+        pass_index(f, a.log_w, a.log_j, o, j, c);
+        const int64_t ib = o * a.in_o + j * a.in_j + c, ob = o * a.out_o + j * a.out_j + c;
+        for (int64_t e = 0; e < n; ++e) x[e] = conj_if(src[ib + e * a.in_e], d.conj_in);
+        if (int rc = run_group(d.log_n, x.data(), x.data(), stw)) return rc;
+        const uint32_t tb = pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj);
+        const uint32_t ts = pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj);
+        for (int64_t k = 0; k < n; ++k) {
+          float2 r = x[k];
+          if (a.log_m > 0) {
+            const uint32_t e = (tb + ts * (uint32_t)k) & mask;
+            r = c_mul(r, four_step_twiddle(tab.lo[a.log_m].data(), tab.hi[a.log_m].data(), e));
+          }
+          dst[ob + k * a.out_e] = epi(r, d.conj_out, a.scale);
+        }
+      }
+      return 0;
+    }
+    case PassKind::RowsT: {
+      const RowsTArgs& a = d.ra;
+      for (int64_t f = 0; f < a.nfft; ++f) {
+        int64_t o, j, c;
+        pass_index(f, a.log_w, a.log_j, o, j, c);
+        const int64_t ib = o * a.in_o + j * a.in_j + c * a.in_c, ob = o * a.out_o + j * a.out_j + c;
+        if (int rc = run_group(d.log_n, src + ib, x.data(), stw)) return rc;
+        for (int64_t k = 0; k < n; ++k) dst[ob + k * a.out_e] = epi(x[k], d.conj_out, a.scale);
+      }
+      return 0;
+    }
+  }
+  return -2;
+}
+
+int run_plan(const PassPlan& pl, const float2* in, float2* out, float2* ws) {
+  float2* bufs[3] = {const_cast<float2*>(in), out, ws};
+  for (int i = 0; i < pl.count; ++i) {
+    const PassDesc& d = pl.p[i];
+    if (int rc = run_pass(d, bufs[(int)d.src], bufs[(int)d.dst])) return rc;
+  }
+  return 0;
 }
 
 }  // namespace
@@ -108,70 +183,22 @@ extern "C" {
 // In-place batched 1D transform, laid out like ferrum_fft_1d_c2c_pow2.
 int emu_fft_1d(float* data, int log_n, int64_t batch, int direction, int normalize) {
   if (log_n < 2 || log_n > kMaxLogN || batch <= 0) return -1;
-  const bool inv = direction < 0;
-  const int64_t n = (int64_t)1 << log_n;
-  const float scale = (inv && normalize) ? 1.0f / (float)n : 1.0f;
+  PassPlan pl = plan_1d(log_n, batch, direction < 0, normalize != 0);
+  std::vector<float2> ws(pl.ws_elems);
   float2* d = (float2*)data;
-  Tables tab(log_n);
-  if (log_n <= kMaxSinglePassLogN) {
-    std::vector<float2> x(n);
-    for (int64_t b = 0; b < batch; ++b) {
-      for (int64_t e = 0; e < n; ++e) x[e] = conj_if(d[b * n + e], inv);
-      int rc = run_group(log_n, x.data(), x.data(), tab.stage[log_n].data());
-      if (rc) return rc;
-      for (int64_t e = 0; e < n; ++e) d[b * n + e] = epi(x[e], inv, scale);
-    }
-    return 0;
-  }
-  const int l1 = four_step_log_n1(log_n), l2 = four_step_log_n2(log_n);
-  const int64_t n1 = (int64_t)1 << l1, n2 = (int64_t)1 << l2;
-  std::vector<float2> ws(n), col(n1), row(n2);
-  for (int64_t b = 0; b < batch; ++b) {
-    float2* xb = d + b * n;
-    // Pass A (fft_cols_kernel with TW4): column n2 of the N1 x N2 view.
-    for (int64_t c = 0; c < n2; ++c) {
-      for (int64_t e = 0; e < n1; ++e) col[e] = conj_if(xb[e * n2 + c], inv);
-      int rc = run_group(l1, col.data(), col.data(), tab.stage[l1].data());
-      if (rc) return rc;
-      for (int64_t k1 = 0; k1 < n1; ++k1)
-        ws[k1 * n2 + c] = c_mul(col[k1], four_step_twiddle(tab.lo.data(), tab.hi.data(),
-                                                           (uint32_t)(c * k1)));
-    }
-    // Pass B (fft_rows_t_kernel): row k1, stored to X[k1 + N1*k2].
-    for (int64_t k1 = 0; k1 < n1; ++k1) {
-      int rc = run_group(l2, ws.data() + k1 * n2, row.data(), tab.stage[l2].data());
-      if (rc) return rc;
-      for (int64_t k2 = 0; k2 < n2; ++k2) xb[k1 + n1 * k2] = epi(row[k2], inv, scale);
-    }
-  }
-  return 0;
+  return run_plan(pl, d, d, ws.data());
 }
+
+// Number of passes the plan for this 1D size uses (for the tests).
+int emu_plan_1d_passes(int log_n) { return plan_1d(log_n, 1, false, false).count; }
 
 // In-place batched 2D transform, laid out like ferrum_fft_2d_c2c_pow2.
 int emu_fft_2d(float* data, int log_n, int64_t batch, int direction, int normalize) {
   if (log_n < 2 || log_n > kMaxSinglePassLogN || batch <= 0) return -1;
-  const bool inv = direction < 0;
-  const int64_t n = (int64_t)1 << log_n;
-  const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
+  PassPlan pl = plan_2d(log_n, batch, direction < 0, normalize != 0);
+  std::vector<float2> ws(pl.ws_elems);
   float2* d = (float2*)data;
-  Tables tab(log_n);
-  const float2* tw = tab.stage[log_n].data();
-  std::vector<float2> x(n);
-  for (int64_t b = 0; b < batch; ++b) {
-    float2* img = d + b * n * n;
-    for (int64_t r = 0; r < n; ++r) {
-      for (int64_t e = 0; e < n; ++e) x[e] = conj_if(img[r * n + e], inv);
-      int rc = run_group(log_n, x.data(), img + r * n, tw);
-      if (rc) return rc;
-    }
-    for (int64_t c = 0; c < n; ++c) {
-      for (int64_t e = 0; e < n; ++e) x[e] = img[e * n + c];
-      int rc = run_group(log_n, x.data(), x.data(), tw);
-      if (rc) return rc;
-      for (int64_t e = 0; e < n; ++e) img[e * n + c] = epi(x[e], inv, scale);
-    }
-  }
-  return 0;
+  return run_plan(pl, d, d, ws.data());
 }
 
 // The distributed 2D transform on `nranks` emulated ranks; `data` is the
@@ -185,41 +212,34 @@ int emu_fft_2d_dist(float* data, int log_n, int nranks, int direction, int norma
   while (((int64_t)1 << lb) < b) ++lb;
   const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
   float2* d = (float2*)data;
-  Tables tab(log_n);
-  const float2* tw = tab.stage[log_n].data();
   std::vector<std::vector<float2>> wa(nranks, std::vector<float2>(b * n)),
       wb(nranks, std::vector<float2>(b * n));
-  std::vector<float2> x(n);
   // 1. row pass, blocked store (fft_rows_kernel with log_block = lb)
-  for (int p = 0; p < nranks; ++p)
-    for (int64_t f = 0; f < b; ++f) {
-      for (int64_t e = 0; e < n; ++e) x[e] = conj_if(d[(p * b + f) * n + e], inv);
-      int rc = run_group(log_n, x.data(), x.data(), tw);
-      if (rc) return rc;
-      for (int64_t e = 0; e < n; ++e) wa[p][blocked_index(f, e, lb, b)] = x[e];
-    }
+  for (int p = 0; p < nranks; ++p) {
+    PassDesc rows = make_rows(log_n, b, inv, false, 1.0f, PassBuf::In, PassBuf::Out, lb);
+    if (int rc = run_pass(rows, d + p * b * n, wa[p].data())) return rc;
+  }
   // 2. all-to-all: block q of rank p -> block p of rank q
   for (int p = 0; p < nranks; ++p)
     for (int q = 0; q < nranks; ++q)
       memcpy(wb[q].data() + p * b * b, wa[p].data() + q * b * b, b * b * sizeof(float2));
-  // 3. column pass in place on the N x B column slab (ld = B)
-  for (int q = 0; q < nranks; ++q)
-    for (int64_t c = 0; c < b; ++c) {
-      for (int64_t e = 0; e < n; ++e) x[e] = wb[q][e * b + c];
-      int rc = run_group(log_n, x.data(), x.data(), tw);
-      if (rc) return rc;
-      for (int64_t e = 0; e < n; ++e) wb[q][e * b + c] = epi(x[e], inv, scale);
-    }
-  // 4. all-to-all of the B x B row blocks
+  // 3. column passes of the N x B column slab: wb -> wa
+  for (int q = 0; q < nranks; ++q) {
+    PassPlan cols;
+    plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::In,
+                 PassBuf::Out);
+    if (int rc = run_plan(cols, wb[q].data(), wa[q].data(), nullptr)) return rc;
+  }
+  // 4. all-to-all of the B x B row blocks: wa -> wb
   for (int p = 0; p < nranks; ++p)
     for (int q = 0; q < nranks; ++q)
-      memcpy(wa[q].data() + p * b * b, wb[p].data() + q * b * b, b * b * sizeof(float2));
+      memcpy(wb[q].data() + p * b * b, wa[p].data() + q * b * b, b * b * sizeof(float2));
   // 5. block gather: out[r][p*B + c] = in[p][r][c]
   for (int q = 0; q < nranks; ++q)
     for (int p = 0; p < nranks; ++p)
       for (int64_t r = 0; r < b; ++r)
         for (int64_t c = 0; c < b; ++c)
-          d[(q * b + r) * n + p * b + c] = wa[q][p * b * b + r * b + c];
+          d[(q * b + r) * n + p * b + c] = wb[q][p * b * b + r * b + c];
   return 0;
 }
 

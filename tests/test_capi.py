@@ -49,11 +49,18 @@ def test_workspace_and_launch_counts(capi):
     assert capi.workspace_bytes(12, 65536, 1) == 0
     assert capi.workspace_bytes(20, 64, 1) == (1 << 20) * 64 * 8
     assert capi.workspace_bytes(24, 4, 1) == (1 << 24) * 4 * 8
-    assert capi.workspace_bytes(12, 16, 2) == 0
+    # 2D up to 1024^2: row pass + one column pass in place; from 2048^2 the
+    # columns run as two sub-passes through an image-sized workspace.
+    assert capi.workspace_bytes(10, 16, 2) == 0
+    assert capi.workspace_bytes(12, 16, 2) == 16 * (1 << 24) * 8
     assert capi.launch_count(10, 256, 1) == 1
     assert capi.launch_count(14, 1, 1) == 1
     assert capi.launch_count(15, 1, 1) == 2
-    assert capi.launch_count(12, 16, 2) == 2
+    assert capi.launch_count(21, 1, 1) == 2
+    assert capi.launch_count(22, 1, 1) == 3
+    assert capi.launch_count(26, 1, 1) == 3
+    assert capi.launch_count(10, 16, 2) == 2
+    assert capi.launch_count(12, 16, 2) == 3
 
 
 @pytest.mark.parametrize("log_n,batch,kind", [(1, 1, 1), (27, 1, 1), (10, 0, 1), (15, 1, 2),

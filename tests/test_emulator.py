@@ -34,30 +34,39 @@ def test_single_pass_matches_oracle(emulator, oracle_mod, log_n, direction, norm
     assert max_rel_err(y, ref) < TOL
 
 
-@pytest.mark.parametrize("log_n", [15, 16, 17, 18, 20])
+@pytest.mark.parametrize("log_n", [15, 16, 17, 18, 20, 21, 22, 23, 24])
 @pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
-def test_four_step_matches_oracle(emulator, oracle_mod, log_n, direction, normalize):
+def test_multi_pass_matches_oracle(emulator, oracle_mod, log_n, direction, normalize):
+    # two passes up to 2^21, three passes from 2^22
     rng = np.random.default_rng(200 + log_n)
-    x = rand_c64(rng, 1 << log_n, "normal")
+    batch = 2 if log_n <= 18 else 1
+    x = rand_c64(rng, batch << log_n, "normal")
     y = x.copy()
-    assert emulator.emu_fft_1d(y.ctypes.data, log_n, 1, _dir(direction), int(normalize)) == 0
-    ref = oracle_mod.fft_1d(x, log_n, direction, normalize, threads=1)
+    assert emulator.emu_fft_1d(y.ctypes.data, log_n, batch, _dir(direction), int(normalize)) == 0
+    ref = oracle_mod.fft_1d(x, log_n, direction, normalize, threads=8)
     assert max_rel_err(y, ref) < TOL
 
 
-@pytest.mark.parametrize("log_n", [2, 3, 4, 5, 6, 8, 10])
+def test_pass_counts(emulator):
+    assert [emulator.emu_plan_1d_passes(l) for l in (2, 14, 15, 21, 22, 26)] == [1, 1, 2, 2, 3, 3]
+
+
+@pytest.mark.parametrize("log_n", [2, 3, 4, 5, 6, 8, 10, 11, 12])
 @pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
 def test_2d_matches_oracle(emulator, oracle_mod, log_n, direction, normalize):
+    # N >= 2048 runs the columns as two sub-passes before the row pass
     rng = np.random.default_rng(300 + log_n)
     n = 1 << log_n
-    x = rand_c64(rng, (2, n, n))
+    x = rand_c64(rng, (2 if log_n <= 10 else 1, n, n))
     y = x.copy()
-    assert emulator.emu_fft_2d(y.ctypes.data, log_n, 2, _dir(direction), int(normalize)) == 0
-    ref = oracle_mod.fft_2d(x, log_n, direction, normalize)
+    assert emulator.emu_fft_2d(y.ctypes.data, log_n, x.shape[0], _dir(direction),
+                               int(normalize)) == 0
+    ref = oracle_mod.fft_2d(x, log_n, direction, normalize, threads=8)
     assert max_rel_err(y, ref) < TOL
 
 
-@pytest.mark.parametrize("log_n,ranks", [(4, 2), (5, 8), (6, 4), (8, 8), (10, 2), (10, 8)])
+@pytest.mark.parametrize("log_n,ranks", [(4, 2), (5, 8), (6, 4), (8, 8), (10, 2), (10, 8),
+                                          (11, 2), (12, 4)])
 @pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
 def test_distributed_2d_decomposition(emulator, oracle_mod, log_n, ranks, direction, normalize):
     rng = np.random.default_rng(400 + log_n + ranks)
@@ -66,5 +75,5 @@ def test_distributed_2d_decomposition(emulator, oracle_mod, log_n, ranks, direct
     y = x.copy()
     assert emulator.emu_fft_2d_dist(y.ctypes.data, log_n, ranks, _dir(direction),
                                     int(normalize)) == 0
-    ref = oracle_mod.fft_2d(x, log_n, direction, normalize)
+    ref = oracle_mod.fft_2d(x, log_n, direction, normalize, threads=8)
     assert max_rel_err(y, ref) < TOL

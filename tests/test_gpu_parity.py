@@ -107,6 +107,24 @@ def test_single_pass_in_place(capi, dev, oracle_mod, log_n):
     assert max_rel_err(got, ref) < TOL
 
 
+@pytest.mark.parametrize("log_n", [4, 8, 12])
+def test_single_pass_unaligned_input_uses_plain_kernel(capi, dev, oracle_mod, log_n):
+    # An input that is 8- but not 16-byte aligned cannot feed the TMA bulk
+    # copies; the call must take the plain kernel and give the same result.
+    rng = np.random.default_rng(3500 + log_n)
+    batch = 600
+    x = rand_c64(rng, batch << log_n)
+    buf = torch.zeros(x.size + 1, dtype=torch.complex64, device="cuda")
+    buf[1:] = torch.from_numpy(x).to("cuda")
+    out = torch.empty(x.size, dtype=torch.complex64, device="cuda")
+    assert (buf[1:].data_ptr() % 16) == 8
+    capi.fft_1d(dev, buf[1:].data_ptr(), out.data_ptr(), log_n, batch, "forward", False, _stream())
+    torch.cuda.synchronize()
+    ref = oracle_mod.fft_1d(x, log_n, threads=8)
+    assert max_rel_err(out.cpu().numpy(), ref) < TOL
+    dev.sync()
+
+
 @pytest.mark.parametrize("log_n", list(range(15, 25)))
 @pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
 def test_four_step(capi, dev, oracle_mod, log_n, direction, normalize):
