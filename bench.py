@@ -90,9 +90,9 @@ def measured_peak():
 
 
 def profiled_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
-    summary (profiles/fft_rows_kernel_4096x8192_full.md), if present."""
-    path = os.path.join(REPO, "profiles", "fft_rows_kernel_4096x8192_full.md")
+    """Per-launch DRAM bytes (read + write) of the dominant kernel, measured by
+    ncu on the full-size launch (profiles/fft_rows_kernel_4096x65536_launches.md)."""
+    path = os.path.join(REPO, "profiles", "fft_rows_kernel_4096x65536_launches.md")
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_launch:"):

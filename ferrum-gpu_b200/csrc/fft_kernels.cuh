@@ -267,7 +267,7 @@ fft_rows_t_kernel(const float2* in, float2* out, const float2* __restrict__ tw, 
   // Transpose FPB rows through shared memory so that lanes run over rows.
   __syncthreads();
 #pragma unroll
-  for (int m = 0; m < G::P; ++m) sm[smem_pad(t + G::T * m)] = v[m];
+  for (int m = 0; m < G::P; ++m) sm[stage_read_addr<LOGN, LOGP>(t, m)] = v[m];
   __syncthreads();
   const int g2 = threadIdx.x % FPB;
   const int e0 = threadIdx.x / FPB;
@@ -280,7 +280,7 @@ fft_rows_t_kernel(const float2* in, float2* out, const float2* __restrict__ tw, 
 #pragma unroll
     for (int q = 0; q < G::P; ++q) {
       const int e = e0 + G::T * q;
-      st_stream(dst + a.out_e * e, epilogue<CONJ_OUT>(row[smem_pad(e)], a.scale));
+      st_stream(dst + a.out_e * e, epilogue<CONJ_OUT>(row[stage_read_addr<LOGN, LOGP>(e0, q)], a.scale));
     }
   }
 }

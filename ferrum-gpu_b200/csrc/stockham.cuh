@@ -58,7 +58,28 @@ FERRUM_HD __forceinline__ void stage_compute(float2 (&v)[1 << LOGP], int t, cons
   constexpr int B = G::P / R;
   constexpr int LNS = plan_log_ns(LOGP, S);
   constexpr int NS = 1 << LNS;
-  if constexpr (S > 0) {
+  if constexpr (S > 0 && R == 16 && B == 1) {
+    // Radix-16 input twiddles w^r, w = W_{16 NS}^k: four table loads (w, w^2,
+    // w^4, w^8) and eleven products instead of fifteen loads. The L1/shared
+    // pipe is the kernel's tightest unit on B200, the FMA pipe has room
+    // (measured +4 % sustained throughput at N = 4096); each power is a
+    // product of at most four correctly rounded table entries.
+    const float2* tws = tw + plan_stage_tw_offset(LOGN, LOGP, S);
+    const int k = t & (NS - 1);
+    float2 w[16];
+    w[1] = tw_load(tws + 0 * NS + k);
+    w[2] = tw_load(tws + 1 * NS + k);
+    w[4] = tw_load(tws + 3 * NS + k);
+    w[8] = tw_load(tws + 7 * NS + k);
+    w[3] = c_mul(w[1], w[2]);
+    w[5] = c_mul(w[1], w[4]);
+    w[6] = c_mul(w[2], w[4]);
+    w[7] = c_mul(w[3], w[4]);
+#pragma unroll
+    for (int r = 9; r < 16; ++r) w[r] = c_mul(w[r - 8], w[8]);
+#pragma unroll
+    for (int r = 1; r < 16; ++r) v[r] = c_mul(v[r], w[r]);
+  } else if constexpr (S > 0) {
     const float2* tws = tw + plan_stage_tw_offset(LOGN, LOGP, S);
 #pragma unroll
     for (int i = 0; i < B; ++i) {
@@ -87,6 +108,43 @@ FERRUM_HD __forceinline__ int stage_out_pos(int t, int i, int r) {
   constexpr int NS = 1 << LNS;
   const int j = t + G::T * i;
   return ((j >> LNS) << (LNS + LR)) + (j & (NS - 1)) + r * NS;
+}
+
+// Padded shared-memory address of output r of butterfly i (thread t) in
+// stage S, as base + r * step. With P = 16, NS is 1 (stage 0, radix R | 16)
+// or a multiple of 16, so pad(pos0 + r*NS) = pad(pos0) + r*step: one address
+// per butterfly and compile-time offsets for the R stores.
+template <int LOGN, int LOGP, int S>
+FERRUM_HD __forceinline__ int stage_write_base(int t, int i) {
+  return smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, 0));
+}
+template <int LOGN, int LOGP, int S>
+FERRUM_HD constexpr int stage_write_step() {
+  return plan_log_ns(LOGP, S) == 0 ? 1
+                                   : (1 << plan_log_ns(LOGP, S)) + ((1 << plan_log_ns(LOGP, S)) >> 4);
+}
+template <int LOGN, int LOGP, int S>
+FERRUM_HD constexpr bool stage_write_affine() {
+  return plan_log_ns(LOGP, S) == 0 ? (16 % (1 << plan_log_radix(LOGN, LOGP, S)) == 0)
+                                   : (plan_log_ns(LOGP, S) >= 4);
+}
+template <int LOGN, int LOGP, int S>
+FERRUM_HD __forceinline__ int stage_write_addr(int t, int i, int r) {
+  if constexpr (stage_write_affine<LOGN, LOGP, S>())
+    return stage_write_base<LOGN, LOGP, S>(t, i) + r * stage_write_step<LOGN, LOGP, S>();
+  else
+    return smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, r));
+}
+
+// Padded shared-memory address of the value thread t reads into slot m
+// (position t + T*m): pad(t) + m*(T + T/16) when T >= 16.
+template <int LOGN, int LOGP>
+FERRUM_HD __forceinline__ int stage_read_addr(int t, int m) {
+  constexpr int T = Geom<LOGN, LOGP>::T;
+  if constexpr (T >= 16)
+    return smem_pad(t) + m * (T + (T >> 4));
+  else
+    return smem_pad(t + T * m);
 }
 
 // Register slot holding output r of butterfly i in stage S.
@@ -125,10 +183,10 @@ __device__ __forceinline__ void run_stages(float2 (&v)[1 << LOGP], float2* sm, i
     for (int i = 0; i < B; ++i)
 #pragma unroll
       for (int r = 0; r < R; ++r)
-        sm[smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, r))] = v[stage_slot<LOGN, LOGP, S>(i, r)];
+        sm[stage_write_addr<LOGN, LOGP, S>(t, i, r)] = v[stage_slot<LOGN, LOGP, S>(i, r)];
     sync();
 #pragma unroll
-    for (int m = 0; m < G::P; ++m) v[m] = sm[smem_pad(t + G::T * m)];
+    for (int m = 0; m < G::P; ++m) v[m] = sm[stage_read_addr<LOGN, LOGP>(t, m)];
     run_stages<LOGN, LOGP, S + 1>(v, sm, t, tw, sync);
   }
 }

@@ -44,14 +44,16 @@ struct Group {
       for (int t = 0; t < G::T; ++t)
         for (int i = 0; i < B; ++i)
           for (int r = 0; r < R; ++r) {
-            const int idx = smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, r));
+            const int idx = stage_write_addr<LOGN, LOGP, S>(t, i, r);
+            if (idx != smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, r))) return -40 - S;
             if (idx < 0 || idx >= slots) return -10 - S;
             sm[idx] = regs[t].v[stage_slot<LOGN, LOGP, S>(i, r)];
             writes[idx]++;
           }
       for (int t = 0; t < G::T; ++t)
         for (int m = 0; m < G::P; ++m) {
-          const int idx = smem_pad(t + G::T * m);
+          const int idx = stage_read_addr<LOGN, LOGP>(t, m);
+          if (idx != smem_pad(t + G::T * m)) return -50 - S;
           if (idx < 0 || idx >= slots || writes[idx] != 1) return -20 - S;
           reads[idx]++;
           regs[t].v[m] = sm[idx];

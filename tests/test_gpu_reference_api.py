@@ -158,15 +158,20 @@ def test_2d_batched_images_and_golden(device, oracle_mod):
         assert max_rel_err(out, oracle_mod.fft_2d(arr, log_n)) < 1e-4
 
 
-def test_kernel_cross_check_inputs(device):
-    # crates/ferrum-gpu-bench/src/bin/kernel-cross-check.rs:33-58 at batch 4
+def test_kernel_cross_check_inputs(device, oracle_mod):
+    # crates/ferrum-gpu-bench/src/bin/kernel-cross-check.rs:20,33-58 at batch 4:
+    # per-bin err / max(|ref|, 1) <= REL_TOL = 1e-3 (the reference's gate; the
+    # CPU oracle itself reaches 1.7e-4 on this metric), plus the suite-wide
+    # max|err| / max|ref| < 1e-4 against both float64 numpy and the oracle.
     for log_n in (8, 10, 12):
         n = 1 << log_n
         t = (np.arange(n * 4) % n).astype(np.float32)
         x = (np.sin(t * np.float32(0.013)) + 1j * np.cos(t * np.float32(0.021))).astype(np.complex64)
         out = fgpu.fft.fft_1d_c2c_pow2(x, log_n, device=device)
         ref = GOLDEN[f"xcheck_{log_n}"]
-        assert float(np.max(np.abs(out - ref) / np.maximum(np.abs(ref), 1.0))) <= 1e-4
+        assert float(np.max(np.abs(out - ref) / np.maximum(np.abs(ref), 1.0))) <= 1e-3
+        assert max_rel_err(out, ref) < 1e-4
+        assert max_rel_err(out, oracle_mod.fft_1d(x, log_n)) < 1e-4
 
 
 def test_input_not_modified_and_noncontiguous(device):
