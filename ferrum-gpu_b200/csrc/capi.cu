@@ -112,7 +112,7 @@ ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* i
     switch (d.kind) {
       case PassKind::Rows:
         e = launch_rows(d.log_n, d.conj_in, d.conj_out, src, dst, stw, d.rows_nfft, d.rows_scale,
-                        stream, d.rows_log_block, dev->err_flag);
+                        stream, d.rows_log_block, dev->err_flag, d.rows_block_rows);
         break;
       case PassKind::Pass: {
         PassArgs a = d.pa;

@@ -2,16 +2,20 @@
 // reference has no multi-GPU code (every context is CudaContext::new(0),
 // crates/ferrum-gpu-py/src/lib.rs:261,385).
 //
-// A single N x N image is split into P row slabs of B = N/P rows. Per call:
-//   1. row FFTs of the local slab; the store writes B x B blocks, one per
-//      destination rank, contiguously ([q][row][col]);
-//   2. NCCL all-to-all: block q goes to rank q. The received blocks, stacked
-//      by source rank, are exactly this rank's N x B column slab, row-major;
+// A single N x N image is split over P ranks (B = N/P) as row slabs or
+// column slabs (dist_steps.h). Row slab in:
+//   1. row FFTs of the local slab, chunk by chunk; the store writes B x B
+//      blocks, one per destination rank ([q][row][col]);
+//   2. NCCL exchange of each chunk as soon as it is written (own stream), so
+//      it overlaps the next chunk's row FFTs. The received blocks, stacked by
+//      source rank, are this rank's N x B column slab, row-major;
 //   3. column FFTs of the column slab (length N, row pitch B), one pass or,
-//      for N >= 2048, two sub-passes with 16 columns per CTA;
-//   4. NCCL all-to-all of the B x B row blocks of the column slab;
-//   5. a block gather turns the received [src][row][col] blocks back into the
-//      row-major B x N output slab.
+//      for N >= 2048, two sub-passes with 16 columns per CTA. With a
+//      column-slab output the transform ends here (one exchange in total);
+//   4. for a row-slab output: exchange of the column slab's B x B row blocks
+//      chunk by chunk, each received chunk gathered into the output rows.
+// Column slab in (the inverse of a column-slab forward): column FFTs, then
+// chunked exchange, gather and row FFTs.
 // NCCL is opened with dlopen so that the single-GPU library never depends on
 // it; when PyTorch is loaded first its libnccl.so.2 is reused. The
 // communicator is non-blocking, so set-up and every host wait are bounded by
@@ -27,6 +31,7 @@
 #include <thread>
 
 #include "fft_kernels.cuh"
+#include "dist_steps.h"
 #include "fft_launch.h"
 #include "passes.h"
 #include "runtime.h"
@@ -38,6 +43,11 @@ struct ferrum_dist_ctx {
   int rank = 0;
   int timeout_ms = 0;
   bool aborted = false;
+  // NCCL runs on its own stream so that the exchange of one chunk of rows
+  // overlaps the kernels of the next; events hand chunks between the streams.
+  cudaStream_t comm_stream = nullptr;
+  static constexpr int kEvents = 16;
+  cudaEvent_t ev[kEvents] = {};
 };
 
 namespace ferrum {
@@ -135,22 +145,31 @@ ferrum_status check_ctx(const ferrum_dist_ctx* ctx) {
   return FERRUM_OK;
 }
 
-// All-to-all of P contiguous blocks of `elems` complex values.
-ferrum_status all_to_all(ferrum_dist_ctx* ctx, const float2* send, float2* recv, int64_t elems,
-                         cudaStream_t stream) {
+// Exchange of rows [r0, r1) of every B x B block (dist_steps.h): to rank q
+// from src + q*B*B + r0*B, from rank p into dst + p*B*B + r0*B.
+ferrum_status all_to_all_rows(ferrum_dist_ctx* ctx, const float2* src, float2* dst, int64_t b,
+                              int64_t r0, int64_t r1, cudaStream_t stream) {
   NcclApi& api = nccl();
+  const size_t count = (size_t)(2 * (r1 - r0) * b);
   ncclResult_t r = api.GroupStart();
   if (r != ncclSuccess) return nccl_error(r, "ncclGroupStart");
   for (int q = 0; q < ctx->nranks; ++q) {
-    r = api.Send(send + q * elems, (size_t)(2 * elems), ncclFloat32, q, ctx->comm, stream);
+    r = api.Send(src + dist_block_offset(q, r0, b), count, ncclFloat32, q, ctx->comm, stream);
     if (r != ncclSuccess && r != ncclInProgress) return nccl_error(r, "ncclSend");
-    r = api.Recv(recv + q * elems, (size_t)(2 * elems), ncclFloat32, q, ctx->comm, stream);
+    r = api.Recv(dst + dist_block_offset(q, r0, b), count, ncclFloat32, q, ctx->comm, stream);
     if (r != ncclSuccess && r != ncclInProgress) return nccl_error(r, "ncclRecv");
   }
   r = api.GroupEnd();
   if (r == ncclInProgress) return wait_comm(ctx, "all-to-all enqueue");
   if (r != ncclSuccess) return nccl_error(r, "ncclGroupEnd");
   return FERRUM_OK;
+}
+
+// `waiter` waits for the work enqueued so far on `from`.
+cudaError_t hand_over(ferrum_dist_ctx* ctx, int slot, cudaStream_t from, cudaStream_t waiter) {
+  cudaError_t e = cudaEventRecord(ctx->ev[slot], from);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(waiter, ctx->ev[slot], 0);
+  return e;
 }
 
 }  // namespace
@@ -224,6 +243,13 @@ ferrum_status ferrum_dist_init(ferrum_device* dev, const unsigned char id[FERRUM
     delete ctx;
     return s;
   }
+  cudaError_t e = cudaStreamCreateWithFlags(&ctx->comm_stream, cudaStreamNonBlocking);
+  for (int i = 0; e == cudaSuccess && i < ferrum_dist_ctx::kEvents; ++i)
+    e = cudaEventCreateWithFlags(&ctx->ev[i], cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    ferrum_dist_destroy(ctx);
+    return cuda_error(e, "dist_init: stream/event creation");
+  }
   *out = ctx;
   return FERRUM_OK;
 }
@@ -232,10 +258,12 @@ ferrum_status ferrum_dist_destroy(ferrum_dist_ctx* ctx) {
   clear_error();
   if (ctx == nullptr) return FERRUM_OK;
   NcclApi& api = nccl();
-  if (ctx->comm && !ctx->aborted && api.ok) {
-    DeviceGuard guard(ctx->dev->ordinal);
-    api.CommDestroy(ctx->comm);
-  }
+  DeviceGuard guard(ctx->dev->ordinal);
+  if (ctx->comm_stream) cudaStreamSynchronize(ctx->comm_stream);
+  if (ctx->comm && !ctx->aborted && api.ok) api.CommDestroy(ctx->comm);
+  for (int i = 0; i < ferrum_dist_ctx::kEvents; ++i)
+    if (ctx->ev[i]) cudaEventDestroy(ctx->ev[i]);
+  if (ctx->comm_stream) cudaStreamDestroy(ctx->comm_stream);
   delete ctx;
   return FERRUM_OK;
 }
@@ -260,30 +288,38 @@ ferrum_status ferrum_dist_workspace_bytes(const ferrum_dist_ctx* ctx, int log_n,
   return FERRUM_OK;
 }
 
-ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx* ctx, const void* in_slab_dev,
-                                          void* out_slab_dev, int log_n, int direction,
-                                          int normalize, void* stream_ptr) {
+ferrum_status ferrum_fft_2d_c2c_pow2_dist_layout(ferrum_dist_ctx* ctx, const void* in_dev,
+                                                 void* out_dev, int log_n, int direction,
+                                                 int normalize, int in_layout, int out_layout,
+                                                 void* stream_ptr) {
   clear_error();
   if (ferrum_status s = check_ctx(ctx)) return s;
   if (ferrum_status s = ferrum_dist_check(log_n, ctx->nranks)) return s;
   if (direction != 1 && direction != -1)
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2_dist: direction must be +1 or -1");
-  if (in_slab_dev == nullptr || out_slab_dev == nullptr)
+  const bool row_in = in_layout == FERRUM_DIST_ROW_SLAB, row_out = out_layout == FERRUM_DIST_ROW_SLAB;
+  if ((in_layout != FERRUM_DIST_ROW_SLAB && in_layout != FERRUM_DIST_COL_SLAB) ||
+      (out_layout != FERRUM_DIST_ROW_SLAB && out_layout != FERRUM_DIST_COL_SLAB) ||
+      (!row_in && !row_out))
+    return set_error(FERRUM_ERR_INVALID_ARG,
+                     "fft_2d_c2c_pow2_dist: layouts must be row->row, row->column or column->row");
+  if (in_dev == nullptr || out_dev == nullptr)
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2_dist: in/out is NULL");
-  if (((uintptr_t)in_slab_dev & 15) || ((uintptr_t)out_slab_dev & 15))
+  if (((uintptr_t)in_dev & 15) || ((uintptr_t)out_dev & 15))
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2_dist: in/out must be 16-byte aligned");
   cudaStream_t stream = (cudaStream_t)stream_ptr;
   ferrum_device* dev = ctx->dev;
   DeviceGuard guard(dev->ordinal);
   if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
   if (ctx->nranks == 1) {
+    // One rank: both layouts are the whole image, row-major.
     const size_t need = workspace_2d_bytes(log_n, 1);
     void* ws1 = nullptr;
     if (need > 0) {
       cudaError_t e = cudaMallocFromPoolAsync(&ws1, need, dev->pool, stream);
       if (e != cudaSuccess) return cuda_error(e, "cudaMallocFromPoolAsync(2D workspace)");
     }
-    ferrum_status s1 = enqueue_2d(dev, (const float2*)in_slab_dev, (float2*)out_slab_dev, log_n, 1,
+    ferrum_status s1 = enqueue_2d(dev, (const float2*)in_dev, (float2*)out_dev, log_n, 1,
                                   direction, normalize != 0, (float2*)ws1, stream);
     if (ws1) cudaFreeAsync(ws1, stream);
     return s1;
@@ -293,8 +329,12 @@ ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx* ctx, const void* in_s
   const int64_t n = (int64_t)1 << log_n;
   const int64_t b = n / ctx->nranks;
   const int lb = ilog2(b);
+  const int chunks = dist_chunks(b);
   const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
   const float2* tw = stage_table(dev, log_n);
+  const float2* in = (const float2*)in_dev;
+  float2* out = (float2*)out_dev;
+  cudaStream_t cs = ctx->comm_stream;
   void* ws = nullptr;
   const size_t slab_bytes = (size_t)(b * n) * sizeof(float2);
   cudaError_t e = cudaMallocFromPoolAsync(&ws, 2 * slab_bytes, dev->pool, stream);
@@ -302,29 +342,82 @@ ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx* ctx, const void* in_s
   float2* wa = (float2*)ws;
   float2* wb = wa + b * n;
   ferrum_status s = FERRUM_OK;
+  int ev = 0;
+  auto cuda_step = [&](cudaError_t err, const char* what) {
+    if (err != cudaSuccess && s == FERRUM_OK) s = cuda_error(err, what);
+    return s == FERRUM_OK;
+  };
   do {
-    e = launch_rows(log_n, inv, false, (const float2*)in_slab_dev, wa, tw, b, 1.0f, stream, lb);
-    if (e != cudaSuccess) {
-      s = cuda_error(e, "distributed row pass launch");
-      break;
-    }
-    if ((s = all_to_all(ctx, wa, wb, b * b, stream)) != FERRUM_OK) break;
-    // Column FFTs of the N x B column slab (row pitch B): wb -> wa, one pass or
-    // two sub-passes (the first in place on wb).
-    PassPlan cols;
-    plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::In,
-                 PassBuf::Out);
-    if ((s = run_plan(dev, cols, wb, wa, nullptr, stream)) != FERRUM_OK) break;
-    if ((s = all_to_all(ctx, wa, wb, b * b, stream)) != FERRUM_OK) break;
-    e = launch_block_gather(wb, (float2*)out_slab_dev, ctx->nranks, b, b, stream);
-    if (e != cudaSuccess) {
-      s = cuda_error(e, "distributed block gather launch");
-      break;
+    if (row_in) {
+      // Row FFTs chunk by chunk, each chunk's blocks exchanged while the next
+      // chunk computes: in -> wa (blocked) -> wb (column slab).
+      for (int c = 0; c < chunks && s == FERRUM_OK; ++c) {
+        int64_t r0, r1;
+        dist_chunk(b, chunks, c, r0, r1);
+        if (!cuda_step(launch_rows(log_n, inv, false, in + r0 * n, wa + r0 * b, tw, r1 - r0, 1.0f,
+                                   stream, lb, nullptr, b),
+                       "distributed row pass launch"))
+          break;
+        if (!cuda_step(hand_over(ctx, ev++, stream, cs), "event")) break;
+        s = all_to_all_rows(ctx, wa, wb, b, r0, r1, cs);
+      }
+      if (s != FERRUM_OK || !cuda_step(hand_over(ctx, ev++, cs, stream), "event")) break;
+      // Column FFTs of the N x B column slab (row pitch B); they apply the
+      // inverse's conjugate and scale.
+      PassPlan cols;
+      plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::In,
+                   PassBuf::Out);
+      if ((s = run_plan(dev, cols, wb, row_out ? wa : out, nullptr, stream)) != FERRUM_OK) break;
+      if (!row_out) break;
+      // Back to row slabs: exchange the column slab's B x B row blocks chunk by
+      // chunk and gather each received chunk into the output rows.
+      if (!cuda_step(hand_over(ctx, ev++, stream, cs), "event")) break;
+      for (int c = 0; c < chunks && s == FERRUM_OK; ++c) {
+        int64_t r0, r1;
+        dist_chunk(b, chunks, c, r0, r1);
+        if ((s = all_to_all_rows(ctx, wa, wb, b, r0, r1, cs)) != FERRUM_OK) break;
+        if (!cuda_step(hand_over(ctx, ev++, cs, stream), "event")) break;
+        cuda_step(launch_block_gather(wb + r0 * b, out + r0 * n, ctx->nranks, r1 - r0, b, b * b, n,
+                                      stream),
+                  "block gather launch");
+      }
+    } else {
+      // Column slab in: column FFTs (in -> wa -> wb), exchange of row blocks,
+      // gather into row slabs and row FFTs, chunk by chunk.
+      PassPlan cols;
+      plan_columns(cols, log_n, lb, b, 1, n * b, inv, false, 1.0f, PassBuf::In, PassBuf::Out,
+                   PassBuf::Ws);
+      if ((s = run_plan(dev, cols, in, wa, wb, stream)) != FERRUM_OK) break;
+      if (!cuda_step(hand_over(ctx, ev++, stream, cs), "event")) break;
+      for (int c = 0; c < chunks && s == FERRUM_OK; ++c) {
+        int64_t r0, r1;
+        dist_chunk(b, chunks, c, r0, r1);
+        if ((s = all_to_all_rows(ctx, wb, wa, b, r0, r1, cs)) != FERRUM_OK) break;
+        if (!cuda_step(hand_over(ctx, ev++, cs, stream), "event")) break;
+        if (!cuda_step(launch_block_gather(wa + r0 * b, out + r0 * n, ctx->nranks, r1 - r0, b,
+                                           b * b, n, stream),
+                       "block gather launch"))
+          break;
+        cuda_step(launch_rows(log_n, false, inv, out + r0 * n, out + r0 * n, tw, r1 - r0, scale,
+                              stream, -1, dev->err_flag),
+                  "distributed row pass launch");
+      }
     }
   } while (false);
+  // The pool memory is released on `stream`, which by now waits for every
+  // exchange that reads or writes it.
+  if (ev > 0 && s != FERRUM_OK) hand_over(ctx, ferrum_dist_ctx::kEvents - 1, cs, stream);
   cudaError_t ef = cudaFreeAsync(ws, stream);
   if (s == FERRUM_OK && ef != cudaSuccess) return cuda_error(ef, "cudaFreeAsync(dist workspace)");
   return s;
+}
+
+ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx* ctx, const void* in_slab_dev,
+                                          void* out_slab_dev, int log_n, int direction,
+                                          int normalize, void* stream) {
+  return ferrum_fft_2d_c2c_pow2_dist_layout(ctx, in_slab_dev, out_slab_dev, log_n, direction,
+                                            normalize, FERRUM_DIST_ROW_SLAB, FERRUM_DIST_ROW_SLAB,
+                                            stream);
 }
 
 ferrum_status ferrum_dist_sync(ferrum_dist_ctx* ctx, void* stream_ptr) {

@@ -74,7 +74,7 @@ template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT>
 __global__ void __launch_bounds__(RowsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::THREADS,
                                   MinBlocks<RowsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::THREADS>::value)
 fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, int64_t nfft,
-                float scale, int log_block) {
+                float scale, int log_block, int64_t block_rows) {
   using G = Geom<LOGN, LOGP>;
   using C = RowsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>;
   extern __shared__ float2 smem[];
@@ -104,11 +104,12 @@ fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, in
       for (int m = 0; m < G::P; ++m) st_stream(dst + G::T * m, epilogue<CONJ_OUT>(v[m], scale));
     } else {
       // Blocked store for the distributed 2D transform: element e of row f goes
-      // to block q = e >> log_block, laid out [q][f][e mod 2^log_block], so
-      // each destination rank's block is contiguous.
+      // to block q = e >> log_block, laid out [q][f][e mod 2^log_block] with
+      // block_rows rows per block, so each destination rank's block is
+      // contiguous (a chunk of rows writes the middle of every block).
 #pragma unroll
       for (int m = 0; m < G::P; ++m)
-        st_stream(out + blocked_index(f, t + G::T * m, log_block, nfft),
+        st_stream(out + blocked_index(f, t + G::T * m, log_block, block_rows),
                   epilogue<CONJ_OUT>(v[m], scale));
     }
   }

@@ -4,6 +4,7 @@
 #include "fft_kernels.cuh"
 #include "fft_launch.h"
 #include "fft_rows_tma.cuh"
+#include "passes.h"
 
 namespace ferrum {
 namespace {
@@ -50,7 +51,7 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 template <int LOGN, bool CI, bool CO>
 cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t nfft, float scale,
-                      int log_block, cudaStream_t s) {
+                      int log_block, int64_t block_rows, cudaStream_t s) {
   constexpr int LOGP = plan_log_p(LOGN);
   constexpr int FPB = rows_fpb(LOGN);
   using C = RowsCfg<LOGN, LOGP, FPB, CI, CO>;
@@ -59,7 +60,8 @@ cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t n
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
   const int64_t blocks = ceil_div(nfft, FPB);
-  k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, log_block);
+  k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, log_block,
+                                                        block_rows);
   return cudaGetLastError();
 }
 
@@ -127,7 +129,7 @@ cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const R
 
 template <int LOGN>
 cudaError_t rows_dispatch(bool ci, bool co, const float2* in, float2* out, const float2* tw,
-                          int64_t nfft, float scale, int lb, int* err, cudaStream_t s) {
+                          int64_t nfft, float scale, int lb, int64_t br, int* err, cudaStream_t s) {
   if constexpr (kRowsTmaEnabled && LOGN >= 4 && LOGN <= 12) {
     // TMA bulk copies need a 16-byte aligned source; blocked stores keep the
     // plain kernel.
@@ -138,22 +140,22 @@ cudaError_t rows_dispatch(bool ci, bool co, const float2* in, float2* out, const
       return rows_tma_impl<LOGN, false, false>(in, out, tw, nfft, scale, err, s);
     }
   }
-  if (ci && co) return rows_impl<LOGN, true, true>(in, out, tw, nfft, scale, lb, s);
-  if (ci) return rows_impl<LOGN, true, false>(in, out, tw, nfft, scale, lb, s);
-  if (co) return rows_impl<LOGN, false, true>(in, out, tw, nfft, scale, lb, s);
-  return rows_impl<LOGN, false, false>(in, out, tw, nfft, scale, lb, s);
+  if (ci && co) return rows_impl<LOGN, true, true>(in, out, tw, nfft, scale, lb, br, s);
+  if (ci) return rows_impl<LOGN, true, false>(in, out, tw, nfft, scale, lb, br, s);
+  if (co) return rows_impl<LOGN, false, true>(in, out, tw, nfft, scale, lb, br, s);
+  return rows_impl<LOGN, false, false>(in, out, tw, nfft, scale, lb, br, s);
 }
 
+// Instantiates exactly the combinations pass_flags_supported() allows.
 template <int LOGN>
 cudaError_t pass_dispatch(bool ci, bool co, bool tw, const float2* in, float2* out,
                           const float2* stw, const PassArgs& a, cudaStream_t s) {
+  if (!pass_flags_supported(ci, co, tw)) return cudaErrorInvalidValue;
   if (tw) {
-    if (co) return cudaErrorInvalidValue;  // a twiddled pass is never the last one
     if (ci) return pass_impl<LOGN, true, false, true>(in, out, stw, a, s);
     return pass_impl<LOGN, false, false, true>(in, out, stw, a, s);
   }
-  if (ci && co) return pass_impl<LOGN, true, true, false>(in, out, stw, a, s);
-  if (ci) return cudaErrorInvalidValue;
+  if (ci) return pass_impl<LOGN, true, false, false>(in, out, stw, a, s);
   if (co) return pass_impl<LOGN, false, true, false>(in, out, stw, a, s);
   return pass_impl<LOGN, false, false, false>(in, out, stw, a, s);
 }
@@ -166,32 +168,38 @@ cudaError_t rows_t_dispatch(bool co, const float2* in, float2* out, const float2
 }
 
 
-// out[r][p*bw + c] = in[p][r][c]; one thread moves two complex values.
+// out[r * out_ld + p*bw + c] = in[p*in_bs + r*bw + c] for p < nblocks, r < rows,
+// c < bw; one thread moves two complex values.
 __global__ void __launch_bounds__(256) block_gather_kernel(const float4* __restrict__ in,
                                                            float4* __restrict__ out,
-                                                           int64_t total2, int64_t rows,
-                                                           int64_t bw2) {
+                                                           int64_t nblocks, int64_t rows,
+                                                           int64_t bw2, int64_t in_bs2,
+                                                           int64_t out_ld2) {
+  const int64_t total2 = nblocks * rows * bw2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total2; i += stride) {
     const int64_t c = i % bw2;
     const int64_t r = (i / bw2) % rows;
     const int64_t p = i / (bw2 * rows);
-    const int64_t nblocks = total2 / (bw2 * rows);
-    out[r * (nblocks * bw2) + p * bw2 + c] = __ldcs(in + i);
+    out[r * out_ld2 + p * bw2 + c] = __ldcs(in + p * in_bs2 + r * bw2 + c);
   }
 }
 
 }  // namespace
 
 cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, int64_t rows,
-                                int64_t bw, cudaStream_t stream) {
-  if (bw % 2 != 0 || ((uintptr_t)in & 15) || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
+                                int64_t bw, int64_t in_block_stride, int64_t out_ld,
+                                cudaStream_t stream) {
+  if (bw % 2 != 0 || in_block_stride % 2 != 0 || out_ld % 2 != 0 || ((uintptr_t)in & 15) ||
+      ((uintptr_t)out & 15))
+    return cudaErrorInvalidValue;
   const int64_t total2 = nblocks * rows * bw / 2;
   int64_t grid = (total2 + 255) / 256;
   if (grid > 148 * 32) grid = 148 * 32;
   if (grid < 1) grid = 1;
-  block_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>((const float4*)in, (float4*)out, total2,
-                                                          rows, bw / 2);
+  block_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>((const float4*)in, (float4*)out, nblocks,
+                                                          rows, bw / 2, in_block_stride / 2,
+                                                          out_ld / 2);
   return cudaGetLastError();
 }
 
@@ -200,13 +208,14 @@ cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, 
 
 cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
                         const float2* tw, int64_t nfft, float scale, cudaStream_t stream,
-                        int log_block, int* err_flag) {
+                        int log_block, int* err_flag, int64_t block_rows) {
   if (log_block < 0 || log_block > log_n) log_block = log_n;
+  if (block_rows <= 0) block_rows = nfft;
   switch (log_n) {
 #define X(L) \
   case L:    \
-    return rows_dispatch<L>(conj_in, conj_out, in, out, tw, nfft, scale, log_block, err_flag, \
-                            stream);
+    return rows_dispatch<L>(conj_in, conj_out, in, out, tw, nfft, scale, log_block, block_rows, \
+                            err_flag, stream);
     FERRUM_CASE_2_14(X)
 #undef X
     default:

@@ -11,22 +11,26 @@ struct RowsTArgs;
 
 // Batched contiguous transforms of length 2^log_n (2 <= log_n <= 14). With
 // 0 <= log_block < log_n the output is stored blocked: element e of row f at
-// (e >> log_block) * nfft * 2^log_block + f * 2^log_block + (e mod 2^log_block).
+// (e >> log_block) * R * 2^log_block + f * 2^log_block + (e mod 2^log_block),
+// R = block_rows (default nfft).
 // With `err_flag` (a device int) and 16 <= N <= 4096, an unblocked store
 // and a 16-byte aligned input, the persistent TMA-prefetch kernel runs; it
 // sets *err_flag if a bounded wait expires.
 cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
                         const float2* tw, int64_t nfft, float scale, cudaStream_t stream,
-                        int log_block = -1, int* err_flag = nullptr);
+                        int log_block = -1, int* err_flag = nullptr, int64_t block_rows = 0);
 
-// Copies `nblocks` row-major (rows x bw) blocks stored one after another into a
-// row-major (rows x nblocks*bw) matrix: out[r][p*bw + c] = in[p][r][c].
+// Gathers `nblocks` row-major (rows x bw) blocks, block p starting at
+// in + p*in_block_stride, into rows of pitch out_ld:
+// out[r*out_ld + p*bw + c] = in[p*in_block_stride + r*bw + c].
 cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, int64_t rows,
-                                int64_t bw, cudaStream_t stream);
+                                int64_t bw, int64_t in_block_stride, int64_t out_ld,
+                                cudaStream_t stream);
 
 // Strided pass (fft_pass_kernel) of length 2^log_n, 2 <= log_n <= 14; with
-// tw the twiddle described by the PassArgs is fused into the store. Supported
-// (conj_in, conj_out, tw): (0,0,0), (0,1,0), (0,0,1), (1,0,1), (1,1,0).
+// tw the twiddle described by the PassArgs is fused into the store. The
+// (conj_in, conj_out, tw) combinations are those pass_flags_supported()
+// (passes.h) accepts; others return cudaErrorInvalidValue.
 cudaError_t launch_pass(int log_n, bool conj_in, bool conj_out, bool tw, const float2* in,
                         float2* out, const float2* stage_tw, const PassArgs& args,
                         cudaStream_t stream);

@@ -39,6 +39,7 @@ struct PassDesc {
   // Rows
   int64_t rows_nfft;
   int rows_log_block;
+  int64_t rows_block_rows;
   float rows_scale;
   // Pass / RowsT (twiddle tables are filled in by the executor from log_m)
   PassArgs pa;
@@ -51,8 +52,15 @@ struct PassPlan {
   int64_t ws_elems = 0;  // workspace (complex values) the plan needs
 };
 
+// (conj_in, conj_out, twiddle) combinations of fft_pass_kernel that are
+// compiled: a twiddled pass is never last (no conj_out), and no single pass
+// both conjugates its input and its output.
+constexpr bool pass_flags_supported(bool ci, bool co, bool tw) {
+  return tw ? !co : !(ci && co);
+}
+
 inline PassDesc make_rows(int log_n, int64_t nfft, bool ci, bool co, float scale, PassBuf src,
-                          PassBuf dst, int log_block = -1) {
+                          PassBuf dst, int log_block = -1, int64_t block_rows = 0) {
   PassDesc d{};
   d.kind = PassKind::Rows;
   d.log_n = log_n;
@@ -62,6 +70,7 @@ inline PassDesc make_rows(int log_n, int64_t nfft, bool ci, bool co, float scale
   d.dst = dst;
   d.rows_nfft = nfft;
   d.rows_log_block = log_block;
+  d.rows_block_rows = block_rows;
   d.rows_scale = scale;
   return d;
 }

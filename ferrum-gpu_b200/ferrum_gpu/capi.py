@@ -26,6 +26,8 @@ FERRUM_ERR_UNSUPPORTED = 6
 FORWARD = 1
 INVERSE = -1
 DIST_ID_BYTES = 128
+DIST_ROW_SLAB = 0
+DIST_COL_SLAB = 1
 
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
@@ -53,6 +55,7 @@ SIGNATURES = {
     "ferrum_dist_world": (_i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "ferrum_dist_workspace_bytes": (_i, [_vp, _i, ctypes.POINTER(_sz)]),
     "ferrum_fft_2d_c2c_pow2_dist": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "ferrum_fft_2d_c2c_pow2_dist_layout": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "ferrum_dist_sync": (_i, [_vp, _vp]),
     "ferrum_dist_check": (_i, [_i, _i]),
 }

@@ -52,6 +52,25 @@ def join_rows(slabs: Sequence):
     return np.concatenate(list(slabs), axis=0)
 
 
+def _layout(name: str) -> int:
+    if name == "rows":
+        return capi.DIST_ROW_SLAB
+    if name == "cols":
+        return capi.DIST_COL_SLAB
+    raise ValueError(f"layout must be 'rows' or 'cols', got {name!r}")
+
+
+def split_cols(image, world: int) -> list:
+    """Column slabs (N x N/P) of an (N, N) array, in rank order (copies)."""
+    n = image.shape[1]
+    out = []
+    for r in range(world):
+        c0, cols = slab_bounds(n, world, r)
+        sl = image[:, c0:c0 + cols]
+        out.append(sl.contiguous() if hasattr(sl, "contiguous") else sl.copy())
+    return out
+
+
 def exchange_unique_id(make_id: Callable[[], bytes], group=None) -> bytes:
     """Rank 0 calls `make_id()`; every rank returns rank 0's bytes."""
     import torch.distributed as dist
@@ -96,26 +115,35 @@ class Dist2D:
         return out.value
 
     def fft_2d(self, in_ptr: int, out_ptr: int, log_n: int, direction="forward",
-               normalize: bool = False, stream: int = 0) -> None:
-        """Enqueue the collective transform of this rank's (N/P) x N slab."""
-        capi.check(capi.lib().ferrum_fft_2d_c2c_pow2_dist(
-            self.ctx, in_ptr, out_ptr, log_n, capi._dir(direction), int(bool(normalize)), stream))
+               normalize: bool = False, stream: int = 0, in_layout: str = "rows",
+               out_layout: str = "rows") -> None:
+        """Enqueue the collective transform. Layout "rows": this rank's
+        (N/P) x N row slab; "cols": its N x (N/P) column slab (columns
+        [rank*N/P, (rank+1)*N/P) of every row). rows->cols and cols->rows need
+        one all-to-all, rows->rows two."""
+        capi.check(capi.lib().ferrum_fft_2d_c2c_pow2_dist_layout(
+            self.ctx, in_ptr, out_ptr, log_n, capi._dir(direction), int(bool(normalize)),
+            _layout(in_layout), _layout(out_layout), stream))
 
     def fft_2d_tensor(self, slab, log_n: int, direction="forward", normalize: bool = False,
-                      out=None):
+                      out=None, in_layout: str = "rows", out_layout: str = "rows"):
         """Torch convenience: `slab` is this rank's contiguous complex64 CUDA
-        tensor of shape (N/P, N). Returns `out` (new tensor by default) after
-        the collective has completed on the current stream."""
+        tensor in `in_layout`. Returns `out` (a new tensor in `out_layout` by
+        default) after the collective has completed on the current stream."""
         import torch
 
         n = 1 << log_n
-        r0, rows = slab_bounds(n, self.world, self.rank)
-        if tuple(slab.shape) != (rows, n) or slab.dtype != torch.complex64 or not slab.is_cuda:
-            raise ValueError(f"slab must be a CUDA complex64 tensor of shape ({rows}, {n})")
+        _, rows = slab_bounds(n, self.world, self.rank)
+        shape = {"rows": (rows, n), "cols": (n, rows)}
+        if (tuple(slab.shape) != shape[in_layout] or slab.dtype != torch.complex64
+                or not slab.is_cuda):
+            raise ValueError(f"slab must be a CUDA complex64 tensor of shape {shape[in_layout]}")
         slab = slab.contiguous()
-        out = torch.empty_like(slab) if out is None else out
+        if out is None:
+            out = torch.empty(shape[out_layout], dtype=torch.complex64, device=slab.device)
         stream = torch.cuda.current_stream().cuda_stream
-        self.fft_2d(slab.data_ptr(), out.data_ptr(), log_n, direction, normalize, stream)
+        self.fft_2d(slab.data_ptr(), out.data_ptr(), log_n, direction, normalize, stream,
+                    in_layout, out_layout)
         self.sync(stream)
         return out
 

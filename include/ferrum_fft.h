@@ -155,6 +155,16 @@ ferrum_status ferrum_dist_workspace_bytes(const ferrum_dist_ctx *ctx, int log_n,
 ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx *ctx, const void *in_slab_dev,
                                           void *out_slab_dev, int log_n, int direction,
                                           int normalize, void *stream);
+/* Layout-aware form: FERRUM_DIST_ROW_SLAB = rank r holds rows [rB, rB+B)
+ * (B x N, row-major); FERRUM_DIST_COL_SLAB = rank r holds columns [rB, rB+B)
+ * of all rows (N x B, row-major). Row -> column needs one all-to-all (the
+ * usual forward), column -> row one (its inverse), row -> row two.
+ * Column -> column is not supported. */
+enum { FERRUM_DIST_ROW_SLAB = 0, FERRUM_DIST_COL_SLAB = 1 };
+ferrum_status ferrum_fft_2d_c2c_pow2_dist_layout(ferrum_dist_ctx *ctx, const void *in_dev,
+                                                 void *out_dev, int log_n, int direction,
+                                                 int normalize, int in_layout, int out_layout,
+                                                 void *stream);
 /* Waits for `stream` with the context's timeout. On timeout or an NCCL error
  * the communicator is aborted and the context becomes unusable. */
 ferrum_status ferrum_dist_sync(ferrum_dist_ctx *ctx, void *stream);

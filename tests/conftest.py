@@ -56,6 +56,9 @@ def emulator():
     lib.emu_fft_2d_dist.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_int]
     lib.emu_fft_2d_dist.restype = ctypes.c_int
+    lib.emu_fft_2d_dist_layout.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.emu_fft_2d_dist_layout.restype = ctypes.c_int
     lib.emu_plan_1d_passes.argtypes = [ctypes.c_int]
     lib.emu_plan_1d_passes.restype = ctypes.c_int
     return lib

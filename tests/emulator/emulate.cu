@@ -16,6 +16,7 @@
 
 #include <vector>
 
+#include "../../ferrum-gpu_b200/csrc/dist_steps.h"
 #include "../../ferrum-gpu_b200/csrc/passes.h"
 #include "../../ferrum-gpu_b200/csrc/twiddle_tables.h"
 
@@ -126,7 +127,8 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst) {
         for (int64_t e = 0; e < n; ++e) x[e] = conj_if(src[f * n + e], d.conj_in);
         if (int rc = run_group(d.log_n, x.data(), x.data(), stw)) return rc;
         for (int64_t e = 0; e < n; ++e) {
-          const int64_t at = lb >= d.log_n ? f * n + e : blocked_index(f, e, lb, d.rows_nfft);
+          const int64_t rows = d.rows_block_rows > 0 ? d.rows_block_rows : d.rows_nfft;
+          const int64_t at = lb >= d.log_n ? f * n + e : blocked_index(f, e, lb, rows);
           dst[at] = epi(x[e], d.conj_out, d.rows_scale);
         }
       }
@@ -134,6 +136,7 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst) {
     }
     case PassKind::Pass: {
       const PassArgs& a = d.pa;
+      if (!pass_flags_supported(d.conj_in, d.conj_out, a.log_m > 0)) return -60;
       const uint32_t mask = a.log_m > 0 ? (1u << a.log_m) - 1u : 0u;
       for (int64_t f = 0; f < a.nfft; ++f) {
         int64_t o, j, c;
@@ -156,6 +159,7 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst) {
     }
     case PassKind::RowsT: {
       const RowsTArgs& a = d.ra;
+      if (d.conj_in || d.log_n < 4) return -61;  // fft_rows_t_kernel: no conj_in, 4 <= log_n <= 14
       for (int64_t f = 0; f < a.nfft; ++f) {
         int64_t o, j, c;
         pass_index(f, a.log_w, a.log_j, o, j, c);
@@ -203,46 +207,101 @@ int emu_fft_2d(float* data, int log_n, int64_t batch, int direction, int normali
   return run_plan(pl, d, d, ws.data());
 }
 
-// The distributed 2D transform on `nranks` emulated ranks; `data` is the
-// whole N x N image, rank p owning rows [p*N/P, (p+1)*N/P).
-int emu_fft_2d_dist(float* data, int log_n, int nranks, int direction, int normalize) {
+// The distributed 2D transform on `nranks` emulated ranks, following the
+// same steps, chunks and offsets as ferrum_fft_2d_c2c_pow2_dist_layout.
+// `data` is the whole N x N image, row-major; it is split into row slabs
+// (layout 0) or column slabs (layout 1) on input and reassembled from the
+// output layout.
+int emu_fft_2d_dist_layout(float* data, int log_n, int nranks, int direction, int normalize,
+                           int in_layout, int out_layout) {
   if (log_n < 2 || log_n > kMaxSinglePassLogN || nranks < 1) return -1;
+  const bool row_in = in_layout == 0, row_out = out_layout == 0;
+  if (!row_in && !row_out) return -1;
   const bool inv = direction < 0;
   const int64_t n = (int64_t)1 << log_n;
   const int64_t b = n / nranks;
   int lb = 0;
   while (((int64_t)1 << lb) < b) ++lb;
+  const int chunks = dist_chunks(b);
   const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
   float2* d = (float2*)data;
-  std::vector<std::vector<float2>> wa(nranks, std::vector<float2>(b * n)),
-      wb(nranks, std::vector<float2>(b * n));
-  // 1. row pass, blocked store (fft_rows_kernel with log_block = lb)
-  for (int p = 0; p < nranks; ++p) {
-    PassDesc rows = make_rows(log_n, b, inv, false, 1.0f, PassBuf::In, PassBuf::Out, lb);
-    if (int rc = run_pass(rows, d + p * b * n, wa[p].data())) return rc;
-  }
-  // 2. all-to-all: block q of rank p -> block p of rank q
+  const size_t slab = (size_t)(b * n);
+  std::vector<std::vector<float2>> in(nranks, std::vector<float2>(slab)),
+      out(nranks, std::vector<float2>(slab)), wa(nranks, std::vector<float2>(slab)),
+      wb(nranks, std::vector<float2>(slab));
   for (int p = 0; p < nranks; ++p)
-    for (int q = 0; q < nranks; ++q)
-      memcpy(wb[q].data() + p * b * b, wa[p].data() + q * b * b, b * b * sizeof(float2));
-  // 3. column passes of the N x B column slab: wb -> wa
-  for (int q = 0; q < nranks; ++q) {
-    PassPlan cols;
-    plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::In,
-                 PassBuf::Out);
-    if (int rc = run_plan(cols, wb[q].data(), wa[q].data(), nullptr)) return rc;
-  }
-  // 4. all-to-all of the B x B row blocks: wa -> wb
-  for (int p = 0; p < nranks; ++p)
-    for (int q = 0; q < nranks; ++q)
-      memcpy(wb[q].data() + p * b * b, wa[p].data() + q * b * b, b * b * sizeof(float2));
-  // 5. block gather: out[r][p*B + c] = in[p][r][c]
-  for (int q = 0; q < nranks; ++q)
+    for (int64_t r = 0; r < (row_in ? b : n); ++r)
+      for (int64_t c = 0; c < (row_in ? n : b); ++c)
+        in[p][r * (row_in ? n : b) + c] = row_in ? d[(p * b + r) * n + c] : d[r * n + p * b + c];
+  // Exchange of rows [r0, r1) of every block: rank p sends from src[p] to q.
+  auto exchange = [&](std::vector<std::vector<float2>>& src, std::vector<std::vector<float2>>& dst,
+                      int64_t r0, int64_t r1) {
     for (int p = 0; p < nranks; ++p)
-      for (int64_t r = 0; r < b; ++r)
-        for (int64_t c = 0; c < b; ++c)
-          d[(q * b + r) * n + p * b + c] = wb[q][p * b * b + r * b + c];
+      for (int q = 0; q < nranks; ++q)
+        memcpy(dst[q].data() + dist_block_offset(p, r0, b), src[p].data() + dist_block_offset(q, r0, b),
+               (size_t)((r1 - r0) * b) * sizeof(float2));
+  };
+  auto gather = [&](const float2* src, float2* dst, int64_t rows) {
+    for (int p = 0; p < nranks; ++p)
+      for (int64_t r = 0; r < rows; ++r)
+        for (int64_t c = 0; c < b; ++c) dst[r * n + p * b + c] = src[p * b * b + r * b + c];
+  };
+  if (row_in) {
+    for (int c = 0; c < chunks; ++c) {
+      int64_t r0, r1;
+      dist_chunk(b, chunks, c, r0, r1);
+      for (int p = 0; p < nranks; ++p) {
+        PassDesc rows = make_rows(log_n, r1 - r0, inv, false, 1.0f, PassBuf::In, PassBuf::Out, lb, b);
+        if (int rc = run_pass(rows, in[p].data() + r0 * n, wa[p].data() + r0 * b)) return rc;
+      }
+      exchange(wa, wb, r0, r1);
+    }
+    for (int p = 0; p < nranks; ++p) {
+      PassPlan cols;
+      plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::In,
+                   PassBuf::Out);
+      if (int rc = run_plan(cols, wb[p].data(), row_out ? wa[p].data() : out[p].data(), nullptr))
+        return rc;
+    }
+    if (row_out)
+      for (int c = 0; c < chunks; ++c) {
+        int64_t r0, r1;
+        dist_chunk(b, chunks, c, r0, r1);
+        exchange(wa, wb, r0, r1);
+        for (int p = 0; p < nranks; ++p) gather(wb[p].data() + r0 * b, out[p].data() + r0 * n, r1 - r0);
+      }
+  } else {
+    for (int p = 0; p < nranks; ++p) {
+      PassPlan cols;
+      plan_columns(cols, log_n, lb, b, 1, n * b, inv, false, 1.0f, PassBuf::In, PassBuf::Out,
+                   PassBuf::Ws);
+      if (int rc = run_plan(cols, in[p].data(), wa[p].data(), wb[p].data())) return rc;
+    }
+    for (int c = 0; c < chunks; ++c) {
+      int64_t r0, r1;
+      dist_chunk(b, chunks, c, r0, r1);
+      exchange(wb, wa, r0, r1);
+      for (int p = 0; p < nranks; ++p) {
+        gather(wa[p].data() + r0 * b, out[p].data() + r0 * n, r1 - r0);
+        PassDesc rows = make_rows(log_n, r1 - r0, false, inv, scale, PassBuf::In, PassBuf::Out);
+        if (int rc = run_pass(rows, out[p].data() + r0 * n, out[p].data() + r0 * n)) return rc;
+      }
+    }
+  }
+  for (int p = 0; p < nranks; ++p)
+    for (int64_t r = 0; r < (row_out ? b : n); ++r)
+      for (int64_t c = 0; c < (row_out ? n : b); ++c) {
+        const float2 v = out[p][r * (row_out ? n : b) + c];
+        if (row_out)
+          d[(p * b + r) * n + c] = v;
+        else
+          d[r * n + p * b + c] = v;
+      }
   return 0;
+}
+
+int emu_fft_2d_dist(float* data, int log_n, int nranks, int direction, int normalize) {
+  return emu_fft_2d_dist_layout(data, log_n, nranks, direction, normalize, 0, 0);
 }
 
 }  // extern "C"
