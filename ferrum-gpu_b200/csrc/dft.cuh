@@ -1,12 +1,13 @@
-// Register-resident forward DFT building blocks (radix 2, 4, 8, 16) on
+// Register-resident forward DFT building blocks (radix 2, 4, 8, 16, 32) on
 // interleaved complex64 values held as float2.
 //
 // Every dft<R>(u) takes u[0..R) in natural order and leaves X[0..R) in natural
 // order, X[k] = sum_n u[n] * exp(-2*pi*i*n*k/R) — the forward sign convention
 // of the reference (crates/ferrum-gpu-fft/src/plan.rs:7-13). Radix 8 is a
 // radix-2 split over two radix-4 DFTs; radix 16 is the 4 x 4 split
-//   X[k1 + 4 k2] = sum_n2 W4^(n2 k2) W16^(n2 k1) sum_n1 u[4 n1 + n2] W4^(n1 k1).
-// The constants below are cos/sin of pi/4 and pi/8.
+//   X[k1 + 4 k2] = sum_n2 W4^(n2 k2) W16^(n2 k1) sum_n1 u[4 n1 + n2] W4^(n1 k1);
+// radix 32 is a radix-2 split over two radix-16 DFTs. The constants are cos
+// and sin of pi/4, pi/8, pi/16 and 3 pi/16.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -103,6 +104,45 @@ FERRUM_HD __forceinline__ void dft16(float2 (&u)[16]) {
   t = u[11]; u[11] = u[14]; u[14] = t;
 }
 
+// cos / sin of pi/16 and 3*pi/16.
+constexpr float kCos16 = 0.98078528040323044913f;
+constexpr float kSin16 = 0.19509032201612826785f;
+constexpr float kCos3_16 = 0.83146961230254523708f;
+constexpr float kSin3_16 = 0.55557023301960222474f;
+
+// Radix 32 = radix-2 split over two radix-16 DFTs:
+// X[k] = E[k] + W32^k O[k], X[k+16] = E[k] - W32^k O[k].
+FERRUM_HD __forceinline__ void dft32(float2 (&u)[32]) {
+  float2 e[16], o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    e[i] = u[2 * i];
+    o[i] = u[2 * i + 1];
+  }
+  dft16(e);
+  dft16(o);
+  o[1] = c_mul(o[1], make_float2(kCos16, -kSin16));
+  o[2] = c_mul(o[2], make_float2(kCos8, -kSin8));
+  o[3] = c_mul(o[3], make_float2(kCos3_16, -kSin3_16));
+  o[4] = c_mul_w8_1(o[4]);
+  o[5] = c_mul(o[5], make_float2(kSin3_16, -kCos3_16));
+  o[6] = c_mul(o[6], make_float2(kSin8, -kCos8));
+  o[7] = c_mul(o[7], make_float2(kSin16, -kCos16));
+  o[8] = c_mul_neg_i(o[8]);
+  o[9] = c_mul(o[9], make_float2(-kSin16, -kCos16));
+  o[10] = c_mul(o[10], make_float2(-kSin8, -kCos8));
+  o[11] = c_mul(o[11], make_float2(-kSin3_16, -kCos3_16));
+  o[12] = c_mul_w8_3(o[12]);
+  o[13] = c_mul(o[13], make_float2(-kCos3_16, -kSin3_16));
+  o[14] = c_mul(o[14], make_float2(-kCos8, -kSin8));
+  o[15] = c_mul(o[15], make_float2(-kCos16, -kSin16));
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    u[k] = c_add(e[k], o[k]);
+    u[k + 16] = c_sub(e[k], o[k]);
+  }
+}
+
 template <int R>
 FERRUM_HD __forceinline__ void dft(float2 (&u)[R]);
 template <> FERRUM_HD __forceinline__ void dft<1>(float2 (&)[1]) {}
@@ -110,5 +150,6 @@ template <> FERRUM_HD __forceinline__ void dft<2>(float2 (&u)[2]) { dft2(u); }
 template <> FERRUM_HD __forceinline__ void dft<4>(float2 (&u)[4]) { dft4(u); }
 template <> FERRUM_HD __forceinline__ void dft<8>(float2 (&u)[8]) { dft8(u); }
 template <> FERRUM_HD __forceinline__ void dft<16>(float2 (&u)[16]) { dft16(u); }
+template <> FERRUM_HD __forceinline__ void dft<32>(float2 (&u)[32]) { dft32(u); }
 
 }  // namespace ferrum

@@ -52,10 +52,13 @@ __device__ __forceinline__ float2 epilogue(float2 v, float scale) {
 }
 
 // Resident CTAs per SM to target: 1024 threads' worth (64 registers per
-// thread), at most 32 CTAs.
-template <int THREADS>
+// thread), at most 32 CTAs; threads owning 32 values get 128 registers.
+template <int THREADS, int LOGP = 4>
 struct MinBlocks {
-  static constexpr int value = (THREADS >= 1024) ? 1 : (1024 / THREADS > 32 ? 32 : 1024 / THREADS);
+  static constexpr int threads_per_sm = LOGP >= 5 ? 512 : 1024;
+  static constexpr int value = (THREADS >= threads_per_sm)
+                                   ? 1
+                                   : (threads_per_sm / THREADS > 32 ? 32 : threads_per_sm / THREADS);
 };
 
 // ----------------------------------------------------------------------------
@@ -72,7 +75,7 @@ struct RowsCfg {
 
 template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT>
 __global__ void __launch_bounds__(RowsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::THREADS,
-                                  MinBlocks<RowsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::THREADS>::value)
+                                  MinBlocks<RowsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::THREADS, LOGP>::value)
 fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, int64_t nfft,
                 float scale, int log_block, int64_t block_rows) {
   using G = Geom<LOGN, LOGP>;
@@ -165,7 +168,7 @@ struct PassCfg {
 
 template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW>
 __global__ void __launch_bounds__(PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS,
-                                  MinBlocks<PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS>::value)
+                                  MinBlocks<PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS, LOGP>::value)
 fft_pass_kernel(const float2* in, float2* out, const float2* __restrict__ tw, PassArgs a) {
   using G = Geom<LOGN, LOGP>;
   using C = PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>;
@@ -238,7 +241,7 @@ struct RowsTCfg {
 
 template <int LOGN, int LOGP, int FPB, bool CONJ_OUT>
 __global__ void __launch_bounds__(RowsTCfg<LOGN, LOGP, FPB, CONJ_OUT>::THREADS,
-                                  MinBlocks<RowsTCfg<LOGN, LOGP, FPB, CONJ_OUT>::THREADS>::value)
+                                  MinBlocks<RowsTCfg<LOGN, LOGP, FPB, CONJ_OUT>::THREADS, LOGP>::value)
 fft_rows_t_kernel(const float2* in, float2* out, const float2* __restrict__ tw, RowsTArgs a) {
   using G = Geom<LOGN, LOGP>;
   using C = RowsTCfg<LOGN, LOGP, FPB, CONJ_OUT>;

@@ -16,6 +16,11 @@ constexpr int kRowsThreads = 256;   // batched rows: 256 threads per CTA up to N
 // element and costs one resident CTA per SM, and the kernel is bound by the
 // L1/shared pipe and issue rate rather than by DRAM latency. It stays off.
 constexpr bool kRowsTmaEnabled = false;
+// Sizes that use fft_rows_pf_kernel (prefetch into the exchange buffer):
+// measured faster only at N = 16384 (0.99 vs 1.11 ms per 2 GiB), where one CTA
+// fills an SM and its load phase was exposed; at N = 8192 (two CTAs per SM)
+// and below it was slower.
+constexpr bool rows_pf_enabled(int log_n) { return log_n == 14; }
 constexpr int kColsThreads = 512;   // strided passes: up to 16 columns / rows per CTA
 
 constexpr int rows_fpb(int log_n) {
@@ -97,6 +102,38 @@ cudaError_t rows_tma_impl(const float2* in, float2* out, const float2* tw, int64
   return cudaGetLastError();
 }
 
+// Persistent rows kernel prefetching into its own exchange buffer
+// (fft_rows_tma.cuh, fft_rows_pf_kernel).
+template <int LOGN, bool CI, bool CO>
+cudaError_t rows_pf_impl(const float2* in, float2* out, const float2* tw, int64_t nfft,
+                         float scale, int* err, cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = rows_fpb(LOGN);
+  using C = RowsPfCfg<LOGN, LOGP, FPB, CI, CO>;
+  auto k = fft_rows_pf_kernel<LOGN, LOGP, FPB, CI, CO>;
+  static std::atomic<uint64_t> smem_done{0};
+  static std::atomic<int> grid_cache[64];
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
+  if (e != cudaSuccess) return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  int resident = grid_cache[dev & 63].load(std::memory_order_relaxed);
+  if (resident == 0) {
+    int per_sm = 0, sms = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, C::THREADS, C::SMEM_BYTES)) !=
+        cudaSuccess)
+      return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return e;
+    resident = (per_sm < 1 ? 1 : per_sm) * sms;
+    grid_cache[dev & 63].store(resident, std::memory_order_relaxed);
+  }
+  const int64_t tiles = ceil_div(nfft, FPB);
+  const int64_t grid = tiles < resident ? tiles : resident;
+  k<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, err);
+  return cudaGetLastError();
+}
+
 template <int LOGN, bool CI, bool CO, bool TW>
 cudaError_t pass_impl(const float2* in, float2* out, const float2* tw, const PassArgs& a,
                       cudaStream_t s) {
@@ -130,6 +167,14 @@ cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const R
 template <int LOGN>
 cudaError_t rows_dispatch(bool ci, bool co, const float2* in, float2* out, const float2* tw,
                           int64_t nfft, float scale, int lb, int64_t br, int* err, cudaStream_t s) {
+  if constexpr (rows_pf_enabled(LOGN)) {
+    if (err != nullptr && lb >= LOGN && ((uintptr_t)in & 15u) == 0) {
+      if (ci && co) return rows_pf_impl<LOGN, true, true>(in, out, tw, nfft, scale, err, s);
+      if (ci) return rows_pf_impl<LOGN, true, false>(in, out, tw, nfft, scale, err, s);
+      if (co) return rows_pf_impl<LOGN, false, true>(in, out, tw, nfft, scale, err, s);
+      return rows_pf_impl<LOGN, false, false>(in, out, tw, nfft, scale, err, s);
+    }
+  }
   if constexpr (kRowsTmaEnabled && LOGN >= 4 && LOGN <= 12) {
     // TMA bulk copies need a 16-byte aligned source; blocked stores keep the
     // plain kernel.

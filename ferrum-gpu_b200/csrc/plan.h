@@ -22,8 +22,15 @@
 
 namespace ferrum {
 
-// Elements owned by one thread: 16 for N >= 16, else N.
-FERRUM_HD constexpr int plan_log_p(int log_n) { return log_n < 4 ? log_n : 4; }
+// Lengths from 2^kLogP32From up give each thread 32 values (radix-32 stages):
+// fewer stages, exchanges and threads per transform where one transform
+// fills an SM.
+constexpr int kLogP32From = 13;
+
+// Elements owned by one thread: N below 16, 32 from 2^kLogP32From, else 16.
+FERRUM_HD constexpr int plan_log_p(int log_n) {
+  return log_n < 4 ? log_n : (log_n >= kLogP32From ? 5 : 4);
+}
 
 FERRUM_HD constexpr int plan_num_stages(int log_n, int log_p) {
   return log_n / log_p + ((log_n % log_p) ? 1 : 0);

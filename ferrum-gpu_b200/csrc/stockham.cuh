@@ -58,12 +58,13 @@ FERRUM_HD __forceinline__ void stage_compute(float2 (&v)[1 << LOGP], int t, cons
   constexpr int B = G::P / R;
   constexpr int LNS = plan_log_ns(LOGP, S);
   constexpr int NS = 1 << LNS;
-  if constexpr (S > 0 && R == 16 && B == 1) {
-    // Radix-16 input twiddles w^r, w = W_{16 NS}^k: four table loads (w, w^2,
-    // w^4, w^8) and eleven products instead of fifteen loads. The L1/shared
-    // pipe is the kernel's tightest unit on B200, the FMA pipe has room
-    // (measured +4 % sustained throughput at N = 4096); each power is a
-    // product of at most four correctly rounded table entries.
+  if constexpr (S > 0 && (R == 16 || R == 32) && B == 1) {
+    // Radix-16/32 input twiddles w^r, w = W_{R NS}^k, from the table entries
+    // w, w^2, w^4, w^8 (and w^16) and products instead of R-1 loads. The
+    // L1/shared pipe is the kernel's tightest unit on B200, the FMA pipe has
+    // room (measured +4 % sustained throughput at N = 4096); each power is a
+    // product of at most five correctly rounded table entries. For radix 32,
+    // w^(16+r) = w^16 * w^r is formed as it is applied, to bound registers.
     const float2* tws = tw + plan_stage_tw_offset(LOGN, LOGP, S);
     const int k = t & (NS - 1);
     float2 w[16];
@@ -79,6 +80,12 @@ FERRUM_HD __forceinline__ void stage_compute(float2 (&v)[1 << LOGP], int t, cons
     for (int r = 9; r < 16; ++r) w[r] = c_mul(w[r - 8], w[8]);
 #pragma unroll
     for (int r = 1; r < 16; ++r) v[r] = c_mul(v[r], w[r]);
+    if constexpr (R == 32) {
+      const float2 w16 = tw_load(tws + 15 * NS + k);
+      v[16] = c_mul(v[16], w16);
+#pragma unroll
+      for (int r = 17; r < 32; ++r) v[r] = c_mul(v[r], c_mul(w16, w[r - 16]));
+    }
   } else if constexpr (S > 0) {
     const float2* tws = tw + plan_stage_tw_offset(LOGN, LOGP, S);
 #pragma unroll
@@ -166,12 +173,19 @@ FERRUM_HD __forceinline__ int64_t blocked_index(int64_t f, int64_t e, int lb, in
 }
 
 #if defined(__CUDACC__)
+struct NoHook {
+  __device__ __forceinline__ void operator()() const {}
+};
+
 // Runs stages S.. to the end. On entry v holds stage S's inputs; on return
 // v[m] = X[t + T*m]. `sm` is this group's padded shared-memory region and
-// `sync` orders the group's shared-memory traffic.
-template <int LOGN, int LOGP, int S, class Sync>
+// `sync` orders the group's shared-memory traffic. `after_last_read` runs (in
+// every thread) once the last exchange has been read, when the shared region
+// is no longer needed.
+template <int LOGN, int LOGP, int S, class Sync, class Hook = NoHook>
 __device__ __forceinline__ void run_stages(float2 (&v)[1 << LOGP], float2* sm, int t,
-                                           const float2* tw, Sync sync) {
+                                           const float2* tw, Sync sync,
+                                           Hook after_last_read = Hook{}) {
   using G = Geom<LOGN, LOGP>;
   stage_compute<LOGN, LOGP, S>(v, t, tw);
   if constexpr (S + 1 < G::STAGES) {
@@ -187,7 +201,8 @@ __device__ __forceinline__ void run_stages(float2 (&v)[1 << LOGP], float2* sm, i
     sync();
 #pragma unroll
     for (int m = 0; m < G::P; ++m) v[m] = sm[stage_read_addr<LOGN, LOGP>(t, m)];
-    run_stages<LOGN, LOGP, S + 1>(v, sm, t, tw, sync);
+    if constexpr (S + 2 == G::STAGES) after_last_read();
+    run_stages<LOGN, LOGP, S + 1>(v, sm, t, tw, sync, after_last_read);
   }
 }
 #endif
