@@ -197,21 +197,15 @@ fft_pass_kernel(const float2* in, float2* out, const float2* __restrict__ tw, Pa
   if (valid) {
     float2* dst = out + o * a.out_o + j * a.out_j + c + (int64_t)t * a.out_e;
     const int64_t step = (int64_t)G::T * a.out_e;
-    uint32_t tb = 0, ts = 0, mask = 0;
     if constexpr (TW) {
-      tb = pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj);
-      ts = pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj);
-      mask = (1u << a.log_m) - 1u;
+      // Output k = t + T*m takes W_M^(tb + ts*k): a progression in m.
+      const uint32_t tb = pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj);
+      const uint32_t ts = pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj);
+      apply_progression_twiddles<G::P>(v, a.tw_lo, a.tw_hi, tb + ts * (uint32_t)t,
+                                       ts * (uint32_t)G::T, (1u << a.log_m) - 1u);
     }
 #pragma unroll
-    for (int m = 0; m < G::P; ++m) {
-      float2 r = v[m];
-      if constexpr (TW) {
-        const uint32_t e = (tb + ts * (uint32_t)(t + G::T * m)) & mask;
-        r = c_mul(r, four_step_twiddle(a.tw_lo, a.tw_hi, e));
-      }
-      st_stream(dst + step * m, epilogue<CONJ_OUT>(r, a.scale));
-    }
+    for (int m = 0; m < G::P; ++m) st_stream(dst + step * m, epilogue<CONJ_OUT>(v[m], a.scale));
   }
 }
 

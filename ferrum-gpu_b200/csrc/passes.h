@@ -12,8 +12,9 @@
 //       1  DFT over n1, times W_{N1 N2}^(n2*k1);
 //       2  DFT over n2, times W_N^(n3*(k1 + N1*k2));
 //       3  DFT over n3 (rows), stored to X[k1 + N1*k2 + N1*N2*k3].
-//   * 2D N x N, N <= 1024: row pass, then one column pass in place.
-//   * 2D, N >= 2048: columns first as two sub-passes (N = A*B, row a + A*b:
+//   * 2D N x N, N <= 2048: row pass, then one column pass in place (N = 2048
+//     reads 32-byte row segments, still near full DRAM efficiency on B200).
+//   * 2D, N >= 4096: columns first as two sub-passes (N = A*B, row a + A*b:
 //     DFT over b times W_N^(a*kb), then DFT over a stored to row kb + B*ka),
 //     then the row pass, which also applies the inverse's conjugate and scale.
 // The index identities are the Cooley-Tukey splits; the reference's CPU
@@ -173,15 +174,20 @@ inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
   return pl;
 }
 
+// Longest column FFT done in one strided pass.
+constexpr int kMaxOnePassColumnLogN = 11;
+
 // Column FFTs of length 2^log_n over `width` adjacent columns (row pitch
 // `ld`), for `images` blocks `img_stride` apart, from `src` to `dst`. One pass
-// when the pass kernel covers >= 8 columns per CTA (N <= 1024), otherwise two
-// sub-passes through `mid`. The last pass applies conj_out / scale.
+// when the pass kernel covers >= 4 columns per CTA with at most 512 threads
+// (N <= 2048), otherwise two sub-passes through `mid`; a one-pass N = 4096
+// column kernel (4 columns, 1024 threads, one CTA per SM) measured slower than
+// the two sub-passes. The last pass applies conj_out / scale.
 inline void plan_columns(PassPlan& pl, int log_n, int log_width, int64_t ld, int64_t images,
                          int64_t img_stride, bool ci, bool co, float scale, PassBuf src,
                          PassBuf mid, PassBuf dst) {
   const int64_t width = (int64_t)1 << log_width;
-  if (log_n <= 10) {
+  if (log_n <= kMaxOnePassColumnLogN) {
     PassArgs a = pass_args(images * width, log_width, 0, img_stride, 0, ld, img_stride, 0, ld);
     a.scale = scale;
     pl.p[pl.count++] = make_pass(log_n, ci, co, src, dst, a);
@@ -207,7 +213,7 @@ inline PassPlan plan_2d(int log_n, int64_t batch, bool inv, bool normalize) {
   const int64_t n = (int64_t)1 << log_n;
   // cpu_2d.rs:56-62: one 1/(n*n) scale computed in float.
   const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
-  if (log_n <= 10) {
+  if (log_n <= kMaxOnePassColumnLogN) {
     pl.p[pl.count++] = make_rows(log_n, batch * n, inv, false, 1.0f, PassBuf::In, PassBuf::Out);
     plan_columns(pl, log_n, log_n, n, batch, n * n, false, inv, scale, PassBuf::Out, PassBuf::Out,
                  PassBuf::Out);

@@ -166,6 +166,38 @@ FERRUM_HD __forceinline__ float2 four_step_twiddle(const float2* lo, const float
                tw_load(lo + (e & ((1u << kFourStepLoBits) - 1))));
 }
 
+// v[m] *= W_M^(e0 + d*m) for m < P (M = mask + 1, a power of two): the
+// twiddles of one thread's outputs k = t + T*m in a strided pass, whose
+// exponents form an arithmetic progression. W_M^e0 and W_M^(d*2^b) come from
+// the two-level table (1 + log2 P lookups instead of P); W_M^(e0 + d*m) is
+// their product over the set bits b of m, at most 1 + log2 P correctly rounded
+// factors. The lookups are what the lanes of a warp gather from scattered
+// addresses, so cutting them relieves the L1 pipe.
+template <int P>
+FERRUM_HD __forceinline__ void apply_progression_twiddles(float2 (&v)[P], const float2* lo,
+                                                          const float2* hi, uint32_t e0,
+                                                          uint32_t d, uint32_t mask) {
+  constexpr int H = P / 2;
+  float2 w[H > 0 ? H : 1];
+  w[0] = four_step_twiddle(lo, hi, e0 & mask);
+  if constexpr (P == 1) {
+    v[0] = c_mul(v[0], w[0]);
+  } else {
+#pragma unroll
+    for (int b = 1; b < H; b <<= 1) {
+      const float2 p = four_step_twiddle(lo, hi, (d * (uint32_t)b) & mask);
+#pragma unroll
+      for (int m = 0; m < b; ++m) w[m + b] = c_mul(w[m], p);
+    }
+    const float2 top = four_step_twiddle(lo, hi, (d * (uint32_t)H) & mask);
+#pragma unroll
+    for (int m = 0; m < H; ++m) {
+      v[m + H] = c_mul(v[m + H], c_mul(w[m], top));
+      v[m] = c_mul(v[m], w[m]);
+    }
+  }
+}
+
 // Blocked layout of the distributed row pass: element e of row f (of nrows)
 // lives at (e >> lb) * nrows * 2^lb + f * 2^lb + (e mod 2^lb).
 FERRUM_HD __forceinline__ int64_t blocked_index(int64_t f, int64_t e, int lb, int64_t nrows) {

@@ -90,6 +90,34 @@ int run_group(int log_n, const float2* x, float2* y, const float2* tw) {
   }
 }
 
+// The strided-pass twiddle epilogue, thread by thread: thread t owns outputs
+// k = t + T*m and multiplies them by W_M^(tb + ts*k) as fft_pass_kernel does.
+template <int LOGN>
+int pass_twiddles_group(float2* x, const float2* lo, const float2* hi, uint32_t tb, uint32_t ts,
+                        uint32_t mask) {
+  using G = Geom<LOGN, plan_log_p(LOGN)>;
+  for (int t = 0; t < G::T; ++t) {
+    float2 v[G::P];
+    for (int m = 0; m < G::P; ++m) v[m] = x[t + G::T * m];
+    apply_progression_twiddles<G::P>(v, lo, hi, tb + ts * (uint32_t)t, ts * (uint32_t)G::T, mask);
+    for (int m = 0; m < G::P; ++m) x[t + G::T * m] = v[m];
+  }
+  return 0;
+}
+
+int apply_pass_twiddles(int log_n, float2* x, const float2* lo, const float2* hi, uint32_t tb,
+                        uint32_t ts, uint32_t mask) {
+  switch (log_n) {
+#define X(L) \
+  case L:    \
+    return pass_twiddles_group<L>(x, lo, hi, tb, ts, mask);
+    X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
+#undef X
+    default:
+      return -1;
+  }
+}
+
 struct Tables {
   std::vector<float2> stage[kMaxSinglePassLogN + 1];
   std::vector<float2> lo[kMaxLogN + 1], hi[kMaxLogN + 1];
@@ -144,16 +172,16 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst) {
         const int64_t ib = o * a.in_o + j * a.in_j + c, ob = o * a.out_o + j * a.out_j + c;
         for (int64_t e = 0; e < n; ++e) x[e] = conj_if(src[ib + e * a.in_e], d.conj_in);
         if (int rc = run_group(d.log_n, x.data(), x.data(), stw)) return rc;
-        const uint32_t tb = pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj);
-        const uint32_t ts = pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj);
-        for (int64_t k = 0; k < n; ++k) {
-          float2 r = x[k];
-          if (a.log_m > 0) {
-            const uint32_t e = (tb + ts * (uint32_t)k) & mask;
-            r = c_mul(r, four_step_twiddle(tab.lo[a.log_m].data(), tab.hi[a.log_m].data(), e));
-          }
-          dst[ob + k * a.out_e] = epi(r, d.conj_out, a.scale);
+        if (a.log_m > 0) {
+          // fft_pass_kernel: thread t owns outputs k = t + T*m and applies
+          // W_M^(tb + ts*k) through apply_progression_twiddles.
+          const uint32_t tb = pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj);
+          const uint32_t ts = pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj);
+          if (int rc = apply_pass_twiddles(d.log_n, x.data(), tab.lo[a.log_m].data(),
+                                           tab.hi[a.log_m].data(), tb, ts, mask))
+            return rc;
         }
+        for (int64_t k = 0; k < n; ++k) dst[ob + k * a.out_e] = epi(x[k], d.conj_out, a.scale);
       }
       return 0;
     }

@@ -60,6 +60,8 @@ def test_workspace_and_launch_counts(capi):
     assert capi.launch_count(22, 1, 1) == 3
     assert capi.launch_count(26, 1, 1) == 3
     assert capi.launch_count(10, 16, 2) == 2
+    assert capi.launch_count(11, 64, 2) == 2
+    assert capi.workspace_bytes(11, 64, 2) == 0
     assert capi.launch_count(12, 16, 2) == 3
 
 

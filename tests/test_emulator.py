@@ -54,7 +54,8 @@ def test_pass_counts(emulator):
 @pytest.mark.parametrize("log_n", [2, 3, 4, 5, 6, 8, 10, 11, 12])
 @pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
 def test_2d_matches_oracle(emulator, oracle_mod, log_n, direction, normalize):
-    # N >= 2048 runs the columns as two sub-passes before the row pass
+    # N = 2048 runs one 4-column strided pass; N >= 4096 runs the columns as two
+    # sub-passes before the row pass
     rng = np.random.default_rng(300 + log_n)
     n = 1 << log_n
     x = rand_c64(rng, (2 if log_n <= 10 else 1, n, n))
