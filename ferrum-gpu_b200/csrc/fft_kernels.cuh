@@ -33,9 +33,9 @@ struct SyncWarp {
 // Per-group shared-memory stride (complex slots). `G` groups share one
 // half-warp (16 lanes, one 128-byte wavefront of 8-byte accesses); a stride
 // congruent to 16/G mod 16 puts their accesses on disjoint bank pairs.
-template <int LOGN, int G>
+template <int LOGN, int LOGP, int G>
 struct RegionStride {
-  static constexpr int base = PaddedLen<LOGN>::value;
+  static constexpr int base = PaddedLen<LOGN, LOGP>::value;
   static constexpr int want = (G <= 1) ? (base & 15) : ((16 / G) & 15);
   static constexpr int value = base + ((want - (base & 15) + 16) & 15);
 };
@@ -68,7 +68,7 @@ struct RowsCfg {
   using G = Geom<LOGN, LOGP>;
   static constexpr int THREADS = FPB * G::T;
   static constexpr int GROUPS_PER_HALFWARP = (G::T >= 16) ? 1 : (16 / G::T);
-  static constexpr int RS = RegionStride<LOGN, GROUPS_PER_HALFWARP>::value;
+  static constexpr int RS = RegionStride<LOGN, LOGP, GROUPS_PER_HALFWARP>::value;
   static constexpr bool NEEDS_SMEM = G::STAGES > 1;
   static constexpr size_t SMEM_BYTES = NEEDS_SMEM ? (size_t)FPB * RS * sizeof(float2) : 0;
 };
@@ -162,7 +162,7 @@ template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW>
 struct PassCfg {
   using G = Geom<LOGN, LOGP>;
   static constexpr int THREADS = FPB * G::T;
-  static constexpr int RS = RegionStride<LOGN, (FPB < 16 ? FPB : 16)>::value;
+  static constexpr int RS = RegionStride<LOGN, LOGP, (FPB < 16 ? FPB : 16)>::value;
   static constexpr size_t SMEM_BYTES = G::STAGES > 1 ? (size_t)FPB * RS * sizeof(float2) : 0;
 };
 
@@ -229,7 +229,7 @@ template <int LOGN, int LOGP, int FPB, bool CONJ_OUT>
 struct RowsTCfg {
   using G = Geom<LOGN, LOGP>;
   static constexpr int THREADS = FPB * G::T;
-  static constexpr int RS = RegionStride<LOGN, (FPB < 16 ? FPB : 16)>::value;
+  static constexpr int RS = RegionStride<LOGN, LOGP, (FPB < 16 ? FPB : 16)>::value;
   static constexpr size_t SMEM_BYTES = (size_t)FPB * RS * sizeof(float2);
 };
 

@@ -79,7 +79,7 @@ struct RowsTmaCfg {
   using G = Geom<LOGN, LOGP>;
   static constexpr int THREADS = FPB * G::T;
   static constexpr int GROUPS_PER_HALFWARP = (G::T >= 16) ? 1 : (16 / G::T);
-  static constexpr int RS = RegionStride<LOGN, GROUPS_PER_HALFWARP>::value;
+  static constexpr int RS = RegionStride<LOGN, LOGP, GROUPS_PER_HALFWARP>::value;
   static constexpr bool NEEDS_XCHG = G::STAGES > 1;
   static constexpr size_t TILE_ELEMS = (size_t)FPB * G::N;
   static constexpr size_t TILE_BYTES = TILE_ELEMS * sizeof(float2);
@@ -178,7 +178,7 @@ template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT>
 struct RowsPfCfg {
   using G = Geom<LOGN, LOGP>;
   static constexpr int THREADS = FPB * G::T;
-  static constexpr int RS = RegionStride<LOGN, 1>::value;
+  static constexpr int RS = RegionStride<LOGN, LOGP, 1>::value;
   static constexpr size_t TILE_ELEMS = (size_t)FPB * G::N;
   static constexpr size_t TILE_BYTES = TILE_ELEMS * sizeof(float2);
   static constexpr size_t XCHG_BYTES = (size_t)FPB * RS * sizeof(float2);

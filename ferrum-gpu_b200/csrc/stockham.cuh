@@ -22,14 +22,19 @@
 
 namespace ferrum {
 
-// Shared-memory padding: one empty slot after every 16 complex values. Stage
-// 0 writes with a stride of 16 values, which would otherwise put a half-warp
-// on a single pair of banks.
-FERRUM_HD __forceinline__ int smem_pad(int i) { return i + (i >> 4); }
+// Shared-memory padding: one empty slot after every 16 complex values, and
+// with 32 values per thread one more after every 32. Stage 0 writes with a
+// stride of P values; unpadded, a half-warp of 8-byte stores would land on
+// one pair of banks. The padded strides, 17 (P = 16) and 35 (P = 32) slots,
+// are odd, so the 16 lanes of a half-warp cover all 32 banks once.
+template <int LOGP>
+FERRUM_HD __forceinline__ constexpr int smem_pad(int i) {
+  return i + (i >> 4) + (LOGP >= 5 ? (i >> 5) : 0);
+}
 
-template <int LOGN>
+template <int LOGN, int LOGP>
 struct PaddedLen {
-  static constexpr int value = (1 << LOGN) + ((1 << LOGN) >> 4);
+  static constexpr int value = smem_pad<LOGP>(1 << LOGN);
 };
 
 FERRUM_HD __forceinline__ float2 tw_load(const float2* p) {
@@ -118,40 +123,37 @@ FERRUM_HD __forceinline__ int stage_out_pos(int t, int i, int r) {
 }
 
 // Padded shared-memory address of output r of butterfly i (thread t) in
-// stage S, as base + r * step. With P = 16, NS is 1 (stage 0, radix R | 16)
-// or a multiple of 16, so pad(pos0 + r*NS) = pad(pos0) + r*step: one address
-// per butterfly and compile-time offsets for the R stores.
+// stage S, as base + offset(r): one address per butterfly and compile-time
+// offsets for the R stores. Stage 0 (NS = 1) writes positions j*R + r with
+// R | 16 or R = 32, so pad(j*R + r) = pad(j*R) + pad(r); later stages have NS
+// a multiple of the padding period (16, or 32 when P = 32), so
+// pad(pos0 + r*NS) = pad(pos0) + r*pad(NS).
 template <int LOGN, int LOGP, int S>
 FERRUM_HD __forceinline__ int stage_write_base(int t, int i) {
-  return smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, 0));
+  return smem_pad<LOGP>(stage_out_pos<LOGN, LOGP, S>(t, i, 0));
 }
 template <int LOGN, int LOGP, int S>
-FERRUM_HD constexpr int stage_write_step() {
-  return plan_log_ns(LOGP, S) == 0 ? 1
-                                   : (1 << plan_log_ns(LOGP, S)) + ((1 << plan_log_ns(LOGP, S)) >> 4);
-}
-template <int LOGN, int LOGP, int S>
-FERRUM_HD constexpr bool stage_write_affine() {
-  return plan_log_ns(LOGP, S) == 0 ? (16 % (1 << plan_log_radix(LOGN, LOGP, S)) == 0)
-                                   : (plan_log_ns(LOGP, S) >= 4);
+FERRUM_HD constexpr int stage_write_offset(int r) {
+  return plan_log_ns(LOGP, S) == 0 ? smem_pad<LOGP>(r)
+                                   : r * smem_pad<LOGP>(1 << plan_log_ns(LOGP, S));
 }
 template <int LOGN, int LOGP, int S>
 FERRUM_HD __forceinline__ int stage_write_addr(int t, int i, int r) {
-  if constexpr (stage_write_affine<LOGN, LOGP, S>())
-    return stage_write_base<LOGN, LOGP, S>(t, i) + r * stage_write_step<LOGN, LOGP, S>();
-  else
-    return smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, r));
+  static_assert(plan_log_ns(LOGP, S) == 0 || plan_log_ns(LOGP, S) >= (LOGP >= 5 ? 5 : 4),
+                "NS must be a multiple of the padding period");
+  return stage_write_base<LOGN, LOGP, S>(t, i) + stage_write_offset<LOGN, LOGP, S>(r);
 }
 
 // Padded shared-memory address of the value thread t reads into slot m
-// (position t + T*m): pad(t) + m*(T + T/16) when T >= 16.
+// (position t + T*m): pad(t) + m*pad(T) when T is a multiple of the padding
+// period.
 template <int LOGN, int LOGP>
 FERRUM_HD __forceinline__ int stage_read_addr(int t, int m) {
   constexpr int T = Geom<LOGN, LOGP>::T;
-  if constexpr (T >= 16)
-    return smem_pad(t) + m * (T + (T >> 4));
+  if constexpr (T % (LOGP >= 5 ? 32 : 16) == 0)
+    return smem_pad<LOGP>(t) + m * smem_pad<LOGP>(T);
   else
-    return smem_pad(t + T * m);
+    return smem_pad<LOGP>(t + T * m);
 }
 
 // Register slot holding output r of butterfly i in stage S.

@@ -39,14 +39,14 @@ struct Group {
       constexpr int LR = plan_log_radix(LOGN, LOGP, S);
       constexpr int R = 1 << LR;
       constexpr int B = G::P / R;
-      const int slots = PaddedLen<LOGN>::value + 16;
+      const int slots = PaddedLen<LOGN, LOGP>::value + 16;
       std::vector<float2> sm(slots);
       std::vector<int> writes(slots, 0), reads(slots, 0);
       for (int t = 0; t < G::T; ++t)
         for (int i = 0; i < B; ++i)
           for (int r = 0; r < R; ++r) {
             const int idx = stage_write_addr<LOGN, LOGP, S>(t, i, r);
-            if (idx != smem_pad(stage_out_pos<LOGN, LOGP, S>(t, i, r))) return -40 - S;
+            if (idx != smem_pad<LOGP>(stage_out_pos<LOGN, LOGP, S>(t, i, r))) return -40 - S;
             if (idx < 0 || idx >= slots) return -10 - S;
             sm[idx] = regs[t].v[stage_slot<LOGN, LOGP, S>(i, r)];
             writes[idx]++;
@@ -54,7 +54,7 @@ struct Group {
       for (int t = 0; t < G::T; ++t)
         for (int m = 0; m < G::P; ++m) {
           const int idx = stage_read_addr<LOGN, LOGP>(t, m);
-          if (idx != smem_pad(t + G::T * m)) return -50 - S;
+          if (idx != smem_pad<LOGP>(t + G::T * m)) return -50 - S;
           if (idx < 0 || idx >= slots || writes[idx] != 1) return -20 - S;
           reads[idx]++;
           regs[t].v[m] = sm[idx];
