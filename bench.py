@@ -2,7 +2,8 @@
 
 Workload (the sweep config at its N=4096 point): batched 1D complex64
 C2C FFT, N = 4096, batch = 65536 per GPU (2 GiB), re/im i.i.d. uniform[-1, 1)
-from a seeded generator. One step = one forward pass (x -> y) and one
+from a seeded generator. ``--log-n L`` runs another point of the sweep
+(single-pass sizes 2 <= L <= 14, batch = 2 GiB / N unless --batch is given). One step = one forward pass (x -> y) and one
 inverse pass with 1/N (y -> z) through the C ABI on device-resident buffers.
 The metric counts 16 bytes per complex element per pass (8 B read + 8 B
 write): GB/s = 2 * 16 * N * batch * ranks / step time. Every buffer (2 GiB)
@@ -46,6 +47,7 @@ METRIC = "batched 1D C2C FFT HBM GB/s"
 UNIT = "GB/s"
 LOG_N = 12
 BATCH = 65536
+TOTAL_ELEMS = 1 << 28  # 2 GiB of complex64 per GPU
 BYTES_PER_ELEM_PASS = 16
 FALLBACK_HBM_GBS = 6650.0
 
@@ -63,19 +65,26 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the secondary measurements (other configs, 2D 16384^2)")
-    ap.add_argument("--batch", type=int, default=BATCH,
-                    help="transforms per GPU (default 65536 = 2 GiB; smaller only for profiling)")
-    return ap.parse_args()
+    ap.add_argument("--log-n", type=int, default=LOG_N, choices=range(2, 15),
+                    help="log2 of the transform length (default 12: the headline N=4096)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="transforms per GPU (default 2 GiB / N; smaller only for profiling)")
+    args = ap.parse_args()
+    if args.batch is None:
+        args.batch = TOTAL_ELEMS >> args.log_n
+    return args
 
 
-def workload_config(batch: int) -> dict:
+def workload_config(log_n: int, batch: int) -> dict:
+    mib = (batch << log_n) * 8 / 2**20
     return {
-        "workload": f"batched 1D C2C forward+inverse(1/N), N={1 << LOG_N}, batch={batch} per GPU "
-                    f"({(batch << LOG_N) * 8 / 2**30:g} GiB complex64), one step = 2 passes",
-        "n": 1 << LOG_N,
+        "workload": f"batched 1D C2C forward+inverse(1/N), N={1 << log_n}, batch={batch} per GPU "
+                    f"({mib / 1024:g} GiB complex64), one step = 2 passes",
+        "n": 1 << log_n,
         "batch_per_gpu": batch,
         "inputs": "re/im i.i.d. uniform[-1,1), seeded",
-        "l2": f"no flush: every buffer is {(batch << LOG_N) * 8 / 2**20:g} MiB > 126 MB L2",
+        "l2": (f"no flush: every buffer is {mib:g} MiB > 126 MB L2" if mib > 126 else
+               f"L2-resident: buffers of {mib:g} MiB fit the 126 MB L2"),
         "bytes_counted": "16 B per complex element per pass",
     }
 
@@ -89,9 +98,12 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic():
+def profiled_traffic(log_n: int, batch: int):
     """Per-launch DRAM bytes (read + write) of the dominant kernel, measured by
-    ncu on the full-size launch (profiles/fft_rows_kernel_4096x65536_launches.md)."""
+    ncu on the full-size launch (profiles/fft_rows_kernel_4096x65536_launches.md);
+    None for workloads without such a capture."""
+    if (log_n, batch) != (LOG_N, BATCH):
+        return None
     path = os.path.join(REPO, "profiles", "fft_rows_kernel_4096x65536_launches.md")
     try:
         for line in open(path):
@@ -122,7 +134,7 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def time_oracle(transforms: int, threads: int, seed: int = 0):
+def time_oracle(transforms: int, threads: int, log_n: int, seed: int = 0):
     """Forward + inverse(1/N) of `transforms` lanes with the oracle; returns
     (seconds, bytes counted)."""
     import numpy as np
@@ -130,35 +142,35 @@ def time_oracle(transforms: int, threads: int, seed: int = 0):
     import oracle
 
     rng = np.random.default_rng(seed)
-    n = 1 << LOG_N
+    n = 1 << log_n
     x = (rng.uniform(-1, 1, transforms * n) + 1j * rng.uniform(-1, 1, transforms * n)).astype(
         np.complex64)
     t0 = time.perf_counter()
-    y = oracle.fft_1d(x, LOG_N, "forward", False, threads=threads)
-    oracle.fft_1d(y, LOG_N, "inverse", True, threads=threads)
+    y = oracle.fft_1d(x, log_n, "forward", False, threads=threads)
+    oracle.fft_1d(y, log_n, "inverse", True, threads=threads)
     dt = time.perf_counter() - t0
     return dt, 2 * BYTES_PER_ELEM_PASS * n * transforms
 
 
-def calibrate_oracle(threads: int) -> float:
+def calibrate_oracle(threads: int, log_n: int) -> float:
     """Seconds per transform (fwd + inv) of the oracle on `threads` threads."""
     probe = max(threads * 4, 64)
-    dt, _ = time_oracle(probe, threads, seed=1)
+    dt, _ = time_oracle(probe, threads, log_n, seed=1)
     return dt / probe
 
 
-def cpu_baseline_leg(target_seconds: float) -> dict:
+def cpu_baseline_leg(target_seconds: float, log_n: int, batch: int) -> dict:
     threads = host_cores()
-    per = calibrate_oracle(threads)
+    per = calibrate_oracle(threads, log_n)
     sample = max(threads, int(target_seconds / max(per, 1e-9)))
-    sample = min(sample, BATCH)
-    dt, nbytes = time_oracle(sample, threads, seed=2)
+    sample = min(sample, batch)
+    dt, nbytes = time_oracle(sample, threads, log_n, seed=2)
     return {
         "value": round(nbytes / dt / 1e9, 3),
         "unit": UNIT,
         "cores": threads,
         "kind": "port",
-        "sample": f"{sample} of the {BATCH} transforms (N={1 << LOG_N}), forward+inverse, "
+        "sample": f"{sample} of the {batch} transforms (N={1 << log_n}), forward+inverse, "
                   f"lane-parallel oracle (C restatement of crates/ferrum-gpu-fft/src/cpu.rs) "
                   f"on {threads} threads, {cpu_model()}; {dt:.1f} s",
     }
@@ -170,20 +182,20 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     threads = host_cores()
-    per = calibrate_oracle(threads)
+    per = calibrate_oracle(threads, args.log_n)
     budget = 90.0
     sample = int(budget / max(per, 1e-9) / max(1, args.steps + args.warmup))
-    sample = max(threads, min(sample, BATCH))
+    sample = max(threads, min(sample, args.batch))
     for w in range(args.warmup):
-        time_oracle(sample, threads, seed=100 + w)
+        time_oracle(sample, threads, args.log_n, seed=100 + w)
     total_t = 0.0
     total_b = 0
     for k in range(args.steps):
-        dt, nb = time_oracle(sample, threads, seed=200 + k)
+        dt, nb = time_oracle(sample, threads, args.log_n, seed=200 + k)
         total_t += dt
         total_b += nb
     value = total_b / total_t / 1e9
-    sample_desc = (f"{sample} of the {BATCH} transforms per step (N={1 << LOG_N}), "
+    sample_desc = (f"{sample} of the {args.batch} transforms per step (N={1 << args.log_n}), "
                    f"forward+inverse(1/N), lane-parallel oracle port of "
                    f"crates/ferrum-gpu-fft/src/cpu.rs on {threads} threads, {cpu_model()}")
     line = {
@@ -200,7 +212,7 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": workload_config(BATCH),
+        "config": workload_config(args.log_n, args.batch),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
                          "kind": "port", "sample": sample_desc},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -371,6 +383,14 @@ def measure_extras(capi, dev, x, y, world, rank, barrier, max_over_ranks) -> dic
     return out
 
 
+def rows_kernel_name(log_n: int) -> str:
+    """The single-pass kernel the library launches for length 2^log_n (the
+    radix plan gives 32 values per thread from N = 8192, 16 below)."""
+    lp = log_n if log_n < 4 else (5 if log_n >= 13 else 4)
+    name = "fft_rows_pf_kernel" if log_n == 14 else "fft_rows_kernel"
+    return f"{name}<{log_n},{lp},*,*,*> (single-pass N={1 << log_n})"
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -397,8 +417,9 @@ def run_ours(args) -> None:
         return float(t.item())
 
     B_ = args.batch
+    L = args.log_n
     dev = capi.DeviceHandle(local)
-    n = 1 << LOG_N
+    n = 1 << L
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     x = torch.complex(torch.rand(B_, n, device="cuda", generator=g) * 2 - 1,
                       torch.rand(B_, n, device="cuda", generator=g) * 2 - 1)
@@ -406,16 +427,16 @@ def run_ours(args) -> None:
     z = torch.empty_like(x)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
-    launches_per_step = 2 * capi.launch_count(LOG_N, B_, 1)
+    launches_per_step = 2 * capi.launch_count(L, B_, 1)
 
     def step(events=None):
         if events is not None:
             events[0].record(stream)
-        capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), LOG_N, B_, "forward", False, sp)
+        capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), L, B_, "forward", False, sp)
         if events is not None:
             events[1].record(stream)
             events[2].record(stream)
-        capi.fft_1d(dev, y.data_ptr(), z.data_ptr(), LOG_N, B_, "inverse", True, sp)
+        capi.fft_1d(dev, y.data_ptr(), z.data_ptr(), L, B_, "inverse", True, sp)
         if events is not None:
             events[3].record(stream)
 
@@ -454,7 +475,7 @@ def run_ours(args) -> None:
     value = world * args.steps * 2 * bytes_per_pass / (elapsed_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = bytes_per_pass / (avg_launch_ms * 1e-3) / 1e9
-    traffic = profiled_traffic()
+    traffic = profiled_traffic(L, B_)
 
     # End to end through the public host-pointer API with pinned buffers.
     e2e = None
@@ -462,12 +483,12 @@ def run_ours(args) -> None:
         hx = x.cpu().pin_memory()
         hy = torch.empty_like(hx).pin_memory()
         hz = torch.empty_like(hx).pin_memory()
-        capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), LOG_N, B_, "forward", False)
+        capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), L, B_, "forward", False)
         barrier()
         t0 = time.perf_counter()
         for _ in range(args.e2e_steps):
-            capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), LOG_N, B_, "forward", False)
-            capi.fft_1d_host(dev, hy.data_ptr(), hz.data_ptr(), LOG_N, B_, "inverse", True)
+            capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), L, B_, "forward", False)
+            capi.fft_1d_host(dev, hy.data_ptr(), hz.data_ptr(), L, B_, "inverse", True)
         t_e2e = max_over_ranks(time.perf_counter() - t0)
         barrier()
         e2e_err = float((hz - hx).abs().max() / hx.abs().max())
@@ -481,13 +502,13 @@ def run_ours(args) -> None:
                "path": "ferrum_fft_1d_c2c_pow2_host (C ABI), pinned host buffers, forward + inverse"}
 
     extras = None
-    if not args.no_extras and B_ == BATCH:
+    if not args.no_extras and (L, B_) == (LOG_N, BATCH):
         extras = measure_extras(capi, dev, x.view(-1), y.view(-1), world, rank, barrier,
                                 max_over_ranks)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_leg(args.cpu_seconds)
+        cpu = cpu_baseline_leg(args.cpu_seconds, L, B_)
 
     if rank == 0:
         line = {
@@ -503,12 +524,12 @@ def run_ours(args) -> None:
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic",
-            "config": workload_config(B_),
+            "config": workload_config(L, B_),
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
             "transforms_per_s": round(world * args.steps * 2 * B_ / (elapsed_ms * 1e-3), 1),
             "roofline": {
                 "bound": "hbm",
-                "kernel": "fft_rows_kernel<12,4,1,*,*> (single-pass N=4096)",
+                "kernel": rows_kernel_name(L),
                 "achieved": round(achieved, 2),
                 "peak": peak,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
