@@ -16,6 +16,22 @@
 //      chunk by chunk, each received chunk gathered into the output rows.
 // Column slab in (the inverse of a column-slab forward): column FFTs, then
 // chunked exchange, gather and row FFTs.
+//
+// Peer-memory path (the default on up to 8 ranks when CUDA IPC works between
+// all of them): every rank holds one receive slab exported with CUDA IPC and
+// mapped by the others, so the exchange is fused into the FFT kernels
+// (dist_kernels.cuh). Row slab in: the row-FFT kernel stores each B x B block
+// straight into the destination rank's slab over NVLink; after a barrier the
+// column passes run on the local slab. Column slab in: column passes into the
+// local slab, a barrier, then a row-FFT kernel that loads its rows from the
+// ranks' slabs. Row -> row adds a peer-load gather of the column results. The
+// barriers are one-CTA kernels on flag words in the same IPC allocations
+// (bounded waits; a timeout sets a device flag that ferrum_dist_sync
+// reports), and every call starts with one so that no rank writes a slab
+// another rank still reads. Set-up agreement: the ranks all-gather their IPC
+// handles and then whether they could map every peer; if any could not (or
+// FERRUM_DIST_P2P=0 is set on any rank) all ranks use the NCCL path.
+//
 // NCCL is opened with dlopen so that the single-GPU library never depends on
 // it; when PyTorch is loaded first its libnccl.so.2 is reused. The
 // communicator is non-blocking, so set-up and every host wait are bounded by
@@ -25,13 +41,17 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <stdlib.h>
+
 #include <chrono>
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
-#include "fft_kernels.cuh"
 #include "dist_steps.h"
+#include "dist_types.h"
+#include "fft_kernels.cuh"
 #include "fft_launch.h"
 #include "passes.h"
 #include "runtime.h"
@@ -48,6 +68,17 @@ struct ferrum_dist_ctx {
   cudaStream_t comm_stream = nullptr;
   static constexpr int kEvents = 16;
   cudaEvent_t ev[kEvents] = {};
+  // Peer-memory path: one cudaMalloc per rank, [flag words | receive slab],
+  // exported with CUDA IPC; peer_base[q] is rank q's allocation as mapped
+  // here (peer_base[rank] = p2p_base).
+  int p2p = -1;  // -1 undecided (decided collectively at the first call), 0 NCCL path, 1 peer path
+  bool p2p_want = true;
+  char* p2p_base = nullptr;
+  size_t p2p_slab_bytes = 0;
+  char* peer_base[ferrum::kMaxPeers] = {};
+  uint32_t epoch = 0;
+  int* err = nullptr;      // device flag: a peer barrier timed out
+  char* stage = nullptr;   // device staging of the set-up all-gathers
 };
 
 namespace ferrum {
@@ -64,6 +95,7 @@ struct NcclApi {
   decltype(&ncclCommAbort) CommAbort = nullptr;
   decltype(&ncclSend) Send = nullptr;
   decltype(&ncclRecv) Recv = nullptr;
+  decltype(&ncclAllGather) AllGather = nullptr;
   decltype(&ncclGroupStart) GroupStart = nullptr;
   decltype(&ncclGroupEnd) GroupEnd = nullptr;
   decltype(&ncclGetErrorString) GetErrorString = nullptr;
@@ -94,6 +126,7 @@ NcclApi& nccl() {
   FERRUM_SYM(CommAbort, ncclCommAbort)
   FERRUM_SYM(Send, ncclSend)
   FERRUM_SYM(Recv, ncclRecv)
+  FERRUM_SYM(AllGather, ncclAllGather)
   FERRUM_SYM(GroupStart, ncclGroupStart)
   FERRUM_SYM(GroupEnd, ncclGroupEnd)
   FERRUM_SYM(GetErrorString, ncclGetErrorString)
@@ -163,6 +196,245 @@ ferrum_status all_to_all_rows(ferrum_dist_ctx* ctx, const float2* src, float2* d
   if (r == ncclInProgress) return wait_comm(ctx, "all-to-all enqueue");
   if (r != ncclSuccess) return nccl_error(r, "ncclGroupEnd");
   return FERRUM_OK;
+}
+
+// Polls `stream` until it drains, bounded by the context's timeout; on
+// timeout or an NCCL error the communicator is aborted.
+ferrum_status wait_stream(ferrum_dist_ctx* ctx, cudaStream_t stream, const char* what) {
+  NcclApi& api = nccl();
+  const auto deadline = Clock::now() + std::chrono::milliseconds(ctx->timeout_ms);
+  for (;;) {
+    cudaError_t e = cudaStreamQuery(stream);
+    if (e == cudaSuccess) return FERRUM_OK;
+    if (e != cudaErrorNotReady) return cuda_error(e, what);
+    ncclResult_t st = ncclSuccess;
+    if (api.CommGetAsyncError(ctx->comm, &st) == ncclSuccess && st != ncclSuccess &&
+        st != ncclInProgress) {
+      api.CommAbort(ctx->comm);
+      ctx->aborted = true;
+      return nccl_error(st, what);
+    }
+    if (Clock::now() > deadline) {
+      api.CommAbort(ctx->comm);
+      ctx->aborted = true;
+      return set_error(FERRUM_ERR_TIMEOUT, std::string(what) + ": timed out after " +
+                                               std::to_string(ctx->timeout_ms) + " ms");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// Reads (and clears) the device flag a timed-out peer barrier sets. After a
+// timeout the ranks are out of step, so the context is marked unusable.
+ferrum_status check_barrier_flag(ferrum_dist_ctx* ctx) {
+  if (ctx->err == nullptr) return FERRUM_OK;
+  int h = 0;
+  cudaError_t e = cudaMemcpy(&h, ctx->err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_error(e, "reading the peer-barrier flag");
+  if (h == 0) return FERRUM_OK;
+  cudaMemset(ctx->err, 0, sizeof(int));
+  NcclApi& api = nccl();
+  if (!ctx->aborted && ctx->comm) api.CommAbort(ctx->comm);
+  ctx->aborted = true;
+  return set_error(FERRUM_ERR_TIMEOUT, "peer barrier: a rank did not arrive within " +
+                                           std::to_string(ctx->timeout_ms) + " ms");
+}
+
+// --- peer-memory path --------------------------------------------------------
+
+constexpr size_t kFlagBytes = 4096;  // flag words ahead of the slab (keeps it 256-byte aligned)
+
+struct PeerRecord {
+  cudaIpcMemHandle_t handle;
+  int32_t ok;
+  char pad[60];
+};
+static_assert(sizeof(PeerRecord) == 128, "PeerRecord layout");
+
+// All-gather of `bytes` per rank through the communicator (stream ordered,
+// then waited for with the context's timeout).
+ferrum_status allgather_host(ferrum_dist_ctx* ctx, const void* mine, void* all, size_t bytes,
+                             cudaStream_t stream) {
+  NcclApi& api = nccl();
+  char* st = ctx->stage;
+  cudaError_t e = cudaMemcpyAsync(st + bytes * ctx->rank, mine, bytes, cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return cuda_error(e, "set-up all-gather staging");
+  ncclResult_t r = api.AllGather(st + bytes * ctx->rank, st, bytes, ncclUint8, ctx->comm, stream);
+  if (r == ncclInProgress) {
+    if (ferrum_status s = wait_comm(ctx, "set-up all-gather")) return s;
+  } else if (r != ncclSuccess) {
+    return nccl_error(r, "ncclAllGather");
+  }
+  e = cudaMemcpyAsync(all, st, bytes * ctx->nranks, cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return cuda_error(e, "set-up all-gather readback");
+  return wait_stream(ctx, stream, "set-up all-gather");
+}
+
+// Host-waited rendezvous of all ranks through the communicator.
+ferrum_status nccl_rendezvous(ferrum_dist_ctx* ctx, cudaStream_t stream, const char* what) {
+  std::vector<int32_t> all(ctx->nranks);
+  const int32_t mine = 1;
+  ferrum_status s = allgather_host(ctx, &mine, all.data(), sizeof(int32_t), stream);
+  if (s != FERRUM_OK) return set_error(s, std::string(what) + ": " + ferrum_last_error());
+  return FERRUM_OK;
+}
+
+// Tears the peer mappings down. `collective`: other ranks have mapped this
+// rank's allocation, so first every rank's device work must be finished (no
+// kernel may still read or write a peer slab), then the ranks unmap, meet
+// again, and only then free: an exporter may free its allocation only after
+// every importer has closed its mapping. The rendezvous go through the
+// communicator, never through peer memory, so a rank that has already left
+// is never written to. When the ranks cannot meet (an aborted communicator)
+// the own allocation is left allocated rather than freed under another
+// rank's mapping.
+void p2p_release(ferrum_dist_ctx* ctx, bool collective, cudaStream_t stream) {
+  bool may_free = !collective;
+  if (collective) {
+    cudaDeviceSynchronize();
+    if (!ctx->aborted) may_free = nccl_rendezvous(ctx, stream, "peer teardown") == FERRUM_OK;
+  }
+  for (int q = 0; q < ctx->nranks && q < kMaxPeers; ++q) {
+    if (q != ctx->rank && ctx->peer_base[q]) cudaIpcCloseMemHandle(ctx->peer_base[q]);
+    ctx->peer_base[q] = nullptr;
+  }
+  if (collective && may_free && !ctx->aborted)
+    may_free = nccl_rendezvous(ctx, stream, "peer teardown") == FERRUM_OK;
+  if (ctx->p2p_base && may_free) cudaFree(ctx->p2p_base);
+  ctx->p2p_base = nullptr;
+  ctx->p2p_slab_bytes = 0;
+  cudaGetLastError();
+}
+
+float2* peer_slab(const ferrum_dist_ctx* ctx, int q) {
+  return reinterpret_cast<float2*>(ctx->peer_base[q] + kFlagBytes);
+}
+
+// Every rank arrives, then every rank proceeds (stream ordered).
+ferrum_status p2p_barrier(ferrum_dist_ctx* ctx, cudaStream_t stream) {
+  PeerFlags flags{};
+  for (int q = 0; q < ctx->nranks; ++q) flags.p[q] = reinterpret_cast<uint32_t*>(ctx->peer_base[q]);
+  const uint64_t timeout_ns = (uint64_t)ctx->timeout_ms * 1000000ull;
+  cudaError_t e = launch_dist_barrier(flags, ctx->rank, ctx->nranks, ++ctx->epoch, timeout_ns,
+                                      ctx->err, stream);
+  return e == cudaSuccess ? FERRUM_OK : cuda_error(e, "peer barrier launch");
+}
+
+// Collective: makes the peer path ready for slabs of `slab_bytes`, or settles
+// on the NCCL path. Every rank calls it with the same size in the same call.
+ferrum_status p2p_prepare(ferrum_dist_ctx* ctx, size_t slab_bytes, cudaStream_t stream) {
+  if (ctx->p2p == 0) return FERRUM_OK;
+  if (ctx->p2p == 1 && ctx->p2p_slab_bytes >= slab_bytes) return FERRUM_OK;
+  // Rebuild (first use, or a larger transform); p2p_release waits until no
+  // rank uses the old mappings.
+  if (ferrum_status s = wait_stream(ctx, stream, "peer set-up")) return s;
+  if (ferrum_status s = check_barrier_flag(ctx)) return s;
+  p2p_release(ctx, ctx->p2p == 1, stream);
+  if (ctx->aborted) return set_error(FERRUM_ERR_NCCL, "peer set-up: communicator aborted");
+  PeerRecord mine{};
+  mine.ok = ctx->p2p_want ? 1 : 0;
+  if (mine.ok) {
+    void* base = nullptr;
+    cudaError_t e = cudaMalloc(&base, kFlagBytes + slab_bytes);
+    if (e == cudaSuccess) {
+      ctx->p2p_base = static_cast<char*>(base);
+      e = cudaMemsetAsync(base, 0, kFlagBytes, stream);
+    }
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine.handle, base);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      mine.ok = 0;
+    }
+  }
+  std::vector<PeerRecord> all(ctx->nranks);
+  if (ferrum_status s = allgather_host(ctx, &mine, all.data(), sizeof(PeerRecord), stream)) {
+    p2p_release(ctx, false, stream);  // no rank has mapped the new allocation yet
+    return s;
+  }
+  int32_t mapped = mine.ok;
+  for (int q = 0; q < ctx->nranks; ++q)
+    if (!all[q].ok) mapped = 0;
+  for (int q = 0; mapped && q < ctx->nranks; ++q) {
+    if (q == ctx->rank) continue;
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, all[q].handle, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      mapped = 0;
+      break;
+    }
+    ctx->peer_base[q] = static_cast<char*>(p);
+  }
+  std::vector<int32_t> oks(ctx->nranks);
+  if (ferrum_status s = allgather_host(ctx, &mapped, oks.data(), sizeof(int32_t), stream)) {
+    p2p_release(ctx, true, stream);  // the communicator is aborted: unmap, keep the allocation
+    return s;
+  }
+  bool everyone = true;
+  for (int32_t v : oks) everyone = everyone && v == 1;
+  if (!everyone) {
+    p2p_release(ctx, true, stream);
+    ctx->p2p = 0;
+    return FERRUM_OK;
+  }
+  ctx->peer_base[ctx->rank] = ctx->p2p_base;
+  ctx->p2p_slab_bytes = slab_bytes;
+  ctx->epoch = 0;
+  ctx->p2p = 1;
+  return FERRUM_OK;
+}
+
+// The transform over peer memory (see the file comment).
+ferrum_status dist_p2p(ferrum_dist_ctx* ctx, const float2* in, float2* out, int log_n, bool inv,
+                       float scale, bool row_in, bool row_out, cudaStream_t stream) {
+  ferrum_device* dev = ctx->dev;
+  const int64_t n = (int64_t)1 << log_n;
+  const int64_t b = n / ctx->nranks;
+  const int lb = ilog2(b);
+  const float2* tw = stage_table(dev, log_n);
+  PeerPtrs blocks{};
+  for (int q = 0; q < ctx->nranks; ++q) blocks.p[q] = peer_slab(ctx, q) + ctx->rank * b * b;
+  float2* mine = peer_slab(ctx, ctx->rank);
+  void* ws = nullptr;
+  if (log_n > kMaxOnePassColumnLogN) {
+    cudaError_t e = cudaMallocFromPoolAsync(&ws, (size_t)(b * n) * sizeof(float2), dev->pool, stream);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMallocFromPoolAsync(dist workspace)");
+  }
+  ferrum_status s = FERRUM_OK;
+  auto launched = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && s == FERRUM_OK) s = cuda_error(e, what);
+    return s == FERRUM_OK;
+  };
+  do {
+    if ((s = p2p_barrier(ctx, stream)) != FERRUM_OK) break;
+    PassPlan cols;
+    if (row_in) {
+      if (!launched(launch_rows_scatter(log_n, inv, in, blocks, tw, b, lb, stream),
+                    "distributed row pass (peer stores)"))
+        break;
+      if ((s = p2p_barrier(ctx, stream)) != FERRUM_OK) break;
+      plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::Ws,
+                   PassBuf::Out);
+      if ((s = run_plan(dev, cols, mine, row_out ? mine : out, (float2*)ws, stream)) != FERRUM_OK)
+        break;
+      if (!row_out) break;
+      if ((s = p2p_barrier(ctx, stream)) != FERRUM_OK) break;
+      launched(launch_peer_block_gather(blocks, out, ctx->nranks, b, b, n, stream),
+               "row-slab gather (peer loads)");
+    } else {
+      plan_columns(cols, log_n, lb, b, 1, n * b, inv, false, 1.0f, PassBuf::In, PassBuf::Ws,
+                   PassBuf::Out);
+      if ((s = run_plan(dev, cols, in, mine, (float2*)ws, stream)) != FERRUM_OK) break;
+      if ((s = p2p_barrier(ctx, stream)) != FERRUM_OK) break;
+      launched(launch_rows_gather(log_n, inv, blocks, out, tw, b, scale, lb, stream),
+               "distributed row pass (peer loads)");
+    }
+  } while (false);
+  if (ws) {
+    cudaError_t ef = cudaFreeAsync(ws, stream);
+    if (s == FERRUM_OK && ef != cudaSuccess) return cuda_error(ef, "cudaFreeAsync(dist workspace)");
+  }
+  return s;
 }
 
 // `waiter` waits for the work enqueued so far on `from`.
@@ -246,6 +518,12 @@ ferrum_status ferrum_dist_init(ferrum_device* dev, const unsigned char id[FERRUM
   cudaError_t e = cudaStreamCreateWithFlags(&ctx->comm_stream, cudaStreamNonBlocking);
   for (int i = 0; e == cudaSuccess && i < ferrum_dist_ctx::kEvents; ++i)
     e = cudaEventCreateWithFlags(&ctx->ev[i], cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->stage, (size_t)nranks * sizeof(PeerRecord));
+  const char* want = getenv("FERRUM_DIST_P2P");
+  ctx->p2p_want = !(want && want[0] == '0');
+  ctx->p2p = (nranks > 1 && nranks <= kMaxPeers) ? -1 : 0;
   if (e != cudaSuccess) {
     ferrum_dist_destroy(ctx);
     return cuda_error(e, "dist_init: stream/event creation");
@@ -260,6 +538,10 @@ ferrum_status ferrum_dist_destroy(ferrum_dist_ctx* ctx) {
   NcclApi& api = nccl();
   DeviceGuard guard(ctx->dev->ordinal);
   if (ctx->comm_stream) cudaStreamSynchronize(ctx->comm_stream);
+  // No rank may unmap or free a slab another rank still uses (p2p_release).
+  p2p_release(ctx, ctx->p2p == 1, ctx->comm_stream);
+  if (ctx->err) cudaFree(ctx->err);
+  if (ctx->stage) cudaFree(ctx->stage);
   if (ctx->comm && !ctx->aborted && api.ok) api.CommDestroy(ctx->comm);
   for (int i = 0; i < ferrum_dist_ctx::kEvents; ++i)
     if (ctx->ev[i]) cudaEventDestroy(ctx->ev[i]);
@@ -331,6 +613,10 @@ ferrum_status ferrum_fft_2d_c2c_pow2_dist_layout(ferrum_dist_ctx* ctx, const voi
   const int lb = ilog2(b);
   const int chunks = dist_chunks(b);
   const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
+  if (ferrum_status sp = p2p_prepare(ctx, (size_t)(b * n) * sizeof(float2), stream)) return sp;
+  if (ctx->p2p == 1)
+    return dist_p2p(ctx, (const float2*)in_dev, (float2*)out_dev, log_n, inv, scale, row_in,
+                    row_out, stream);
   const float2* tw = stage_table(dev, log_n);
   const float2* in = (const float2*)in_dev;
   float2* out = (float2*)out_dev;
@@ -420,32 +706,47 @@ ferrum_status ferrum_fft_2d_c2c_pow2_dist(ferrum_dist_ctx* ctx, const void* in_s
                                             stream);
 }
 
+ferrum_status ferrum_dist_barrier(ferrum_dist_ctx* ctx, void* stream_ptr) {
+  clear_error();
+  if (ferrum_status s = check_ctx(ctx)) return s;
+  DeviceGuard guard(ctx->dev->ordinal);
+  cudaStream_t stream = (cudaStream_t)stream_ptr;
+  if (ctx->nranks == 1) return FERRUM_OK;
+  if (ctx->p2p == 1) return p2p_barrier(ctx, stream);
+  NcclApi& api = nccl();
+  ncclResult_t r = api.AllGather(ctx->stage + sizeof(int32_t) * ctx->rank, ctx->stage,
+                                 sizeof(int32_t), ncclUint8, ctx->comm, stream);
+  if (r == ncclInProgress) return wait_comm(ctx, "dist_barrier");
+  return r == ncclSuccess ? FERRUM_OK : nccl_error(r, "dist_barrier");
+}
+
+int ferrum_dist_peer_path(const ferrum_dist_ctx* ctx) { return ctx ? ctx->p2p : -2; }
+
+ferrum_status ferrum_dist_abort(ferrum_dist_ctx* ctx) {
+  clear_error();
+  if (ctx == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, "dist_abort: NULL ctx");
+  if (!ctx->aborted) {
+    NcclApi& api = nccl();
+    if (ctx->comm && api.ok) api.CommAbort(ctx->comm);
+    ctx->aborted = true;
+  }
+  return FERRUM_OK;
+}
+
+ferrum_status ferrum_dist_set_timeout(ferrum_dist_ctx* ctx, int timeout_ms) {
+  clear_error();
+  if (ctx == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, "dist_set_timeout: NULL ctx");
+  if (timeout_ms <= 0) return set_error(FERRUM_ERR_INVALID_ARG, "dist_set_timeout: timeout_ms must be > 0");
+  ctx->timeout_ms = timeout_ms;
+  return FERRUM_OK;
+}
+
 ferrum_status ferrum_dist_sync(ferrum_dist_ctx* ctx, void* stream_ptr) {
   clear_error();
   if (ferrum_status s = check_ctx(ctx)) return s;
   DeviceGuard guard(ctx->dev->ordinal);
-  NcclApi& api = nccl();
-  cudaStream_t stream = (cudaStream_t)stream_ptr;
-  const auto deadline = Clock::now() + std::chrono::milliseconds(ctx->timeout_ms);
-  for (;;) {
-    cudaError_t e = cudaStreamQuery(stream);
-    if (e == cudaSuccess) return FERRUM_OK;
-    if (e != cudaErrorNotReady) return cuda_error(e, "dist_sync");
-    ncclResult_t st = ncclSuccess;
-    if (api.CommGetAsyncError(ctx->comm, &st) == ncclSuccess && st != ncclSuccess &&
-        st != ncclInProgress) {
-      api.CommAbort(ctx->comm);
-      ctx->aborted = true;
-      return nccl_error(st, "dist_sync");
-    }
-    if (Clock::now() > deadline) {
-      api.CommAbort(ctx->comm);
-      ctx->aborted = true;
-      return set_error(FERRUM_ERR_TIMEOUT, "dist_sync: timed out after " +
-                                               std::to_string(ctx->timeout_ms) + " ms");
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
-  }
+  if (ferrum_status s = wait_stream(ctx, (cudaStream_t)stream_ptr, "dist_sync")) return s;
+  return check_barrier_flag(ctx);
 }
 
 }  // extern "C"

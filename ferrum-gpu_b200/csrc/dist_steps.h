@@ -17,6 +17,8 @@
 
 #include <stdint.h>
 
+#include "plan.h"
+
 namespace ferrum {
 
 inline int64_t dist_block_offset(int64_t peer, int64_t r0, int64_t b) { return peer * b * b + r0 * b; }
@@ -28,5 +30,12 @@ inline void dist_chunk(int64_t b, int chunks, int c, int64_t& r0, int64_t& r1) {
 }
 
 inline int dist_chunks(int64_t b) { return b >= 4 ? 4 : (int)b; }
+
+// Peer-memory path: element e of local row f of rank p lives in rank
+// (e >> log_b)'s receive slab (its N x B column slab) at
+// p*B*B + peer_offset(f, e, log_b), i.e. row p*B + f, column e mod B.
+FERRUM_HD inline int64_t peer_offset(int64_t f, int64_t e, int log_b) {
+  return (f << log_b) + (e & (((int64_t)1 << log_b) - 1));
+}
 
 }  // namespace ferrum

@@ -1,6 +1,7 @@
 // Template dispatch from runtime (log_n, direction flags) to the pass kernels.
 #include <atomic>
 
+#include "dist_kernels.cuh"
 #include "fft_kernels.cuh"
 #include "fft_launch.h"
 #include "fft_rows_tma.cuh"
@@ -213,6 +214,35 @@ cudaError_t rows_t_dispatch(bool co, const float2* in, float2* out, const float2
 }
 
 
+template <int LOGN, bool CI>
+cudaError_t rows_scatter_impl(const float2* in, const PeerPtrs& dst, const float2* tw,
+                              int64_t nfft, int log_b, cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = rows_fpb(LOGN);
+  using C = RowsCfg<LOGN, LOGP, FPB, CI, false>;
+  auto k = fft_rows_scatter_kernel<LOGN, LOGP, FPB, CI>;
+  static std::atomic<uint64_t> smem_done{0};
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
+  if (e != cudaSuccess) return e;
+  k<<<(unsigned)ceil_div(nfft, FPB), C::THREADS, C::SMEM_BYTES, s>>>(in, dst, tw, nfft, log_b);
+  return cudaGetLastError();
+}
+
+template <int LOGN, bool CO>
+cudaError_t rows_gather_impl(const PeerPtrs& src, float2* out, const float2* tw, int64_t nfft,
+                             float scale, int log_b, cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = rows_fpb(LOGN);
+  using C = RowsCfg<LOGN, LOGP, FPB, false, CO>;
+  auto k = fft_rows_gather_kernel<LOGN, LOGP, FPB, CO>;
+  static std::atomic<uint64_t> smem_done{0};
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
+  if (e != cudaSuccess) return e;
+  k<<<(unsigned)ceil_div(nfft, FPB), C::THREADS, C::SMEM_BYTES, s>>>(src, out, tw, nfft, scale,
+                                                                     log_b);
+  return cudaGetLastError();
+}
+
 // out[r * out_ld + p*bw + c] = in[p*in_bs + r*bw + c] for p < nblocks, r < rows,
 // c < bw; one thread moves two complex values.
 __global__ void __launch_bounds__(256) block_gather_kernel(const float4* __restrict__ in,
@@ -245,6 +275,62 @@ cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, 
   block_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>((const float4*)in, (float4*)out, nblocks,
                                                           rows, bw / 2, in_block_stride / 2,
                                                           out_ld / 2);
+  return cudaGetLastError();
+}
+
+#define FERRUM_CASE_4_14(X) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
+
+cudaError_t launch_rows_scatter(int log_n, bool conj_in, const float2* in, const PeerPtrs& dst,
+                                const float2* tw, int64_t nfft, int log_b, cudaStream_t stream) {
+  if (log_b < 1 || log_b > log_n) return cudaErrorInvalidValue;
+  switch (log_n) {
+#define X(L)                                                                        \
+  case L:                                                                           \
+    return conj_in ? rows_scatter_impl<L, true>(in, dst, tw, nfft, log_b, stream)   \
+                   : rows_scatter_impl<L, false>(in, dst, tw, nfft, log_b, stream);
+    FERRUM_CASE_4_14(X)
+#undef X
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_rows_gather(int log_n, bool conj_out, const PeerPtrs& src, float2* out,
+                               const float2* tw, int64_t nfft, float scale, int log_b,
+                               cudaStream_t stream) {
+  if (log_b < 1 || log_b > log_n) return cudaErrorInvalidValue;
+  switch (log_n) {
+#define X(L)                                                                                  \
+  case L:                                                                                     \
+    return conj_out ? rows_gather_impl<L, true>(src, out, tw, nfft, scale, log_b, stream)     \
+                    : rows_gather_impl<L, false>(src, out, tw, nfft, scale, log_b, stream);
+    FERRUM_CASE_4_14(X)
+#undef X
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_peer_block_gather(const PeerPtrs& src, float2* out, int nranks, int64_t rows,
+                                     int64_t b, int64_t out_ld, cudaStream_t stream) {
+  if (nranks < 1 || nranks > kMaxPeers || b % 2 != 0 || out_ld % 2 != 0 || ((uintptr_t)out & 15))
+    return cudaErrorInvalidValue;
+  for (int q = 0; q < nranks; ++q)
+    if ((uintptr_t)src.p[q] & 15) return cudaErrorInvalidValue;
+  const int64_t total2 = (int64_t)nranks * rows * b / 2;
+  int64_t grid = (total2 + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  if (grid < 1) grid = 1;
+  peer_block_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>(src, (float4*)out, nranks, rows,
+                                                               b / 2, out_ld / 2);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dist_barrier(const PeerFlags& flags, int rank, int nranks, uint32_t epoch,
+                                uint64_t timeout_ns, int* err, cudaStream_t stream) {
+  if (nranks < 1 || nranks > kMaxPeers || rank < 0 || rank >= nranks || err == nullptr)
+    return cudaErrorInvalidValue;
+  dist_barrier_kernel<<<1, 32, 0, stream>>>(flags, rank, nranks, epoch, timeout_ns, err);
   return cudaGetLastError();
 }
 

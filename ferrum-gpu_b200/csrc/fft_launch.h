@@ -8,14 +8,16 @@ namespace ferrum {
 
 struct PassArgs;
 struct RowsTArgs;
+struct PeerPtrs;
+struct PeerFlags;
 
 // Batched contiguous transforms of length 2^log_n (2 <= log_n <= 14). With
 // 0 <= log_block < log_n the output is stored blocked: element e of row f at
 // (e >> log_block) * R * 2^log_block + f * 2^log_block + (e mod 2^log_block),
 // R = block_rows (default nfft).
-// With `err_flag` (a device int) and 16 <= N <= 4096, an unblocked store
-// and a 16-byte aligned input, the persistent TMA-prefetch kernel runs; it
-// sets *err_flag if a bounded wait expires.
+// With `err_flag` (a device int), N = 16384, an unblocked store and a
+// 16-byte aligned input, the persistent prefetching kernel runs; it sets
+// *err_flag if a bounded wait expires.
 cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
                         const float2* tw, int64_t nfft, float scale, cudaStream_t stream,
                         int log_block = -1, int* err_flag = nullptr, int64_t block_rows = 0);
@@ -38,5 +40,22 @@ cudaError_t launch_pass(int log_n, bool conj_in, bool conj_out, bool tw, const f
 // Rows of length 2^log_n (4 <= log_n <= 14) stored transposed.
 cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* out,
                           const float2* tw, const RowsTArgs& args, cudaStream_t stream);
+
+// Distributed 2D over peer memory (dist_kernels.cuh); 4 <= log_n <= 14,
+// B = 2^log_b columns per rank. Row FFTs of `nfft` local rows whose output
+// element e goes to dst.p[e >> log_b] + f*B + (e mod B):
+cudaError_t launch_rows_scatter(int log_n, bool conj_in, const float2* in, const PeerPtrs& dst,
+                                const float2* tw, int64_t nfft, int log_b, cudaStream_t stream);
+// Row FFTs whose input element e of row f comes from
+// src.p[e >> log_b] + f*B + (e mod B); contiguous output rows.
+cudaError_t launch_rows_gather(int log_n, bool conj_out, const PeerPtrs& src, float2* out,
+                               const float2* tw, int64_t nfft, float scale, int log_b,
+                               cudaStream_t stream);
+// out[r*out_ld + q*B + c] = src.p[q][r*B + c] (q < nranks, r < rows, c < B).
+cudaError_t launch_peer_block_gather(const PeerPtrs& src, float2* out, int nranks, int64_t rows,
+                                     int64_t b, int64_t out_ld, cudaStream_t stream);
+// Cross-GPU barrier through peer flag words; sets *err after timeout_ns.
+cudaError_t launch_dist_barrier(const PeerFlags& flags, int rank, int nranks, uint32_t epoch,
+                                uint64_t timeout_ns, int* err, cudaStream_t stream);
 
 }  // namespace ferrum

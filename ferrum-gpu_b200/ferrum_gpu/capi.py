@@ -57,6 +57,10 @@ SIGNATURES = {
     "ferrum_fft_2d_c2c_pow2_dist": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "ferrum_fft_2d_c2c_pow2_dist_layout": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "ferrum_dist_sync": (_i, [_vp, _vp]),
+    "ferrum_dist_barrier": (_i, [_vp, _vp]),
+    "ferrum_dist_peer_path": (_i, [_vp]),
+    "ferrum_dist_set_timeout": (_i, [_vp, _i]),
+    "ferrum_dist_abort": (_i, [_vp]),
     "ferrum_dist_check": (_i, [_i, _i]),
 }
 

@@ -7,11 +7,15 @@ passes its slab to :meth:`Dist2D.fft_2d` and gets its slab of the 2D result
 back. The data path (row FFTs, NCCL all-to-all, column FFTs, all-to-all,
 block gather) runs in libferrum_fft.so (ferrum_fft_2d_c2c_pow2_dist);
 Python only sets up the communicator: rank 0 creates the NCCL unique id and
-``torch.distributed`` broadcasts it.
+``torch.distributed`` broadcasts it. On up to 8 ranks whose GPUs can map each
+other's memory the library fuses the exchange into the FFT kernels (peer
+stores and loads over NVLink, :attr:`Dist2D.peer_path` is 1 after the first
+transform); otherwise, or with ``FERRUM_DIST_P2P=0``, NCCL moves the blocks.
 
-Failure handling: communicator set-up and :meth:`Dist2D.sync` are bounded
-by ``timeout_ms``; on expiry the communicator is aborted and
-:class:`ferrum_gpu.capi.FerrumError` (status FERRUM_ERR_TIMEOUT) is raised.
+Failure handling: communicator set-up, :meth:`Dist2D.sync` and the device-side
+peer barriers are bounded by ``timeout_ms``; on expiry the communicator is
+aborted and :class:`ferrum_gpu.capi.FerrumError` (status FERRUM_ERR_TIMEOUT)
+is raised by the next :meth:`Dist2D.sync`.
 A rank that never reaches set-up makes the id broadcast fail after the
 process group's own timeout.
 """
@@ -149,6 +153,24 @@ class Dist2D:
 
     def sync(self, stream: int = 0) -> None:
         capi.check(capi.lib().ferrum_dist_sync(self.ctx, stream))
+
+    def barrier(self, stream: int = 0) -> None:
+        """Stream-ordered barrier across the ranks (collective)."""
+        capi.check(capi.lib().ferrum_dist_barrier(self.ctx, stream))
+
+    def abort(self) -> None:
+        """Abandon the collective without waiting for other ranks (after a
+        peer failure learned on the host); close() then frees local state."""
+        capi.check(capi.lib().ferrum_dist_abort(self.ctx))
+
+    def set_timeout(self, timeout_ms: int) -> None:
+        """Bound for later waits and device-side peer barriers."""
+        capi.check(capi.lib().ferrum_dist_set_timeout(self.ctx, int(timeout_ms)))
+
+    @property
+    def peer_path(self) -> int:
+        """1: exchange over peer memory, 0: NCCL, -1: not decided yet."""
+        return int(capi.lib().ferrum_dist_peer_path(self.ctx))
 
     def close(self) -> None:
         if getattr(self, "ctx", None):

@@ -129,11 +129,15 @@ ferrum_status ferrum_fft_workspace_bytes(int log_n, size_t batch, int kind, size
 ferrum_status ferrum_fft_launch_count(int log_n, size_t batch, int kind, int *launches);
 
 /* ---------------------------------------------------------------------------
- * Distributed 2D (one process per GPU, NCCL over NVLink). New in this build:
- * the reference is single-GPU. A single N x N image is split into row slabs
- * of N/P rows; each rank holds its slab row-major. Row FFTs run locally, an
- * NCCL all-to-all moves (N/P) x (N/P) blocks, column FFTs run on the
- * received column slab, and a second all-to-all returns row slabs.
+ * Distributed 2D (one process per GPU over NVLink). New in this build: the
+ * reference is single-GPU. A single N x N image is split into row slabs of
+ * N/P rows; each rank holds its slab row-major. On up to 8 ranks whose GPUs
+ * can map each other's memory (CUDA IPC) the exchange is fused into the FFT
+ * kernels: the row-FFT kernel stores each (N/P) x (N/P) block directly into
+ * the destination rank's receive slab, the column FFTs run on the received
+ * column slab, and the return to row slabs is a row-FFT (or copy) kernel
+ * that loads from the ranks' slabs. Otherwise (or with FERRUM_DIST_P2P=0 in
+ * the environment of any rank) an NCCL all-to-all moves the blocks.
  */
 typedef struct ferrum_dist_ctx ferrum_dist_ctx;
 
@@ -165,9 +169,29 @@ ferrum_status ferrum_fft_2d_c2c_pow2_dist_layout(ferrum_dist_ctx *ctx, const voi
                                                  void *out_dev, int log_n, int direction,
                                                  int normalize, int in_layout, int out_layout,
                                                  void *stream);
-/* Waits for `stream` with the context's timeout. On timeout or an NCCL error
- * the communicator is aborted and the context becomes unusable. */
+/* Waits for `stream` with the context's timeout. On timeout, an NCCL error or
+ * a peer barrier that timed out on the device (FERRUM_ERR_TIMEOUT) the
+ * communicator is aborted and the context becomes unusable. */
 ferrum_status ferrum_dist_sync(ferrum_dist_ctx *ctx, void *stream);
+/* Collective, stream ordered: no rank's work after it on `stream` starts
+ * before every rank's work before it has finished. On the peer-memory path a
+ * one-CTA kernel on flag words in peer memory whose wait is bounded by the
+ * context's timeout (expiry is reported by ferrum_dist_sync); on the NCCL
+ * path a 4-byte all-gather. No counterpart in the reference. */
+ferrum_status ferrum_dist_barrier(ferrum_dist_ctx *ctx, void *stream);
+/* Which data path the context uses: 1 = peer memory (CUDA IPC over NVLink,
+ * exchange fused into the FFT kernels), 0 = NCCL send/recv, -1 = not decided
+ * yet (it is decided collectively by the first transform), -2 = NULL ctx. */
+int ferrum_dist_peer_path(const ferrum_dist_ctx *ctx);
+/* Host-side abort, for a rank that learns by its own means (a process group,
+ * a heartbeat) that another rank has failed: aborts the communicator without
+ * waiting for any rank; the context is unusable afterwards and
+ * ferrum_dist_destroy then only releases local resources (a peer-memory slab
+ * other ranks may still map is left allocated, not freed under them). */
+ferrum_status ferrum_dist_abort(ferrum_dist_ctx *ctx);
+/* Replaces the timeout that bounds later host waits and device-side peer
+ * barriers (set-up often needs a longer bound than the steady state). */
+ferrum_status ferrum_dist_set_timeout(ferrum_dist_ctx *ctx, int timeout_ms);
 /* FERRUM_OK when (log_n, nranks) is a supported distributed shape: nranks a
  * power of two, log_n in [4, 14], N / nranks >= 2. */
 ferrum_status ferrum_dist_check(int log_n, int nranks);

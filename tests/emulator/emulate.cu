@@ -240,6 +240,84 @@ int emu_fft_2d(float* data, int log_n, int64_t batch, int direction, int normali
 // `data` is the whole N x N image, row-major; it is split into row slabs
 // (layout 0) or column slabs (layout 1) on input and reassembled from the
 // output layout.
+// The peer-memory path of dist.cu (dist_p2p): each rank's receive slab is
+// written by the row-FFT scatter (or read by the row-FFT gather) through
+// peer_offset, the column passes run on the local slab.
+int emu_fft_2d_dist_p2p(float* data, int log_n, int nranks, int direction, int normalize,
+                        int in_layout, int out_layout) {
+  if (log_n < 4 || log_n > kMaxSinglePassLogN || nranks < 1) return -1;
+  const bool row_in = in_layout == 0, row_out = out_layout == 0;
+  if (!row_in && !row_out) return -1;
+  const bool inv = direction < 0;
+  const int64_t n = (int64_t)1 << log_n;
+  const int64_t b = n / nranks;
+  int lb = 0;
+  while (((int64_t)1 << lb) < b) ++lb;
+  const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
+  const float2* stw = tables().stage[log_n].data();
+  float2* d = (float2*)data;
+  const size_t slab = (size_t)(b * n);
+  std::vector<std::vector<float2>> in(nranks, std::vector<float2>(slab)),
+      out(nranks, std::vector<float2>(slab)), recv(nranks, std::vector<float2>(slab)),
+      ws(nranks, std::vector<float2>(slab));
+  for (int p = 0; p < nranks; ++p)
+    for (int64_t r = 0; r < (row_in ? b : n); ++r)
+      for (int64_t c = 0; c < (row_in ? n : b); ++c)
+        in[p][r * (row_in ? n : b) + c] = row_in ? d[(p * b + r) * n + c] : d[r * n + p * b + c];
+  std::vector<float2> x(n);
+  if (row_in) {
+    // fft_rows_scatter_kernel on every rank, then the barrier.
+    for (int p = 0; p < nranks; ++p)
+      for (int64_t f = 0; f < b; ++f) {
+        for (int64_t e = 0; e < n; ++e) {
+          const float2 v = in[p][f * n + e];
+          x[e] = inv ? make_float2(v.x, -v.y) : v;  // CONJ_IN of the scatter kernel
+        }
+        if (int rc = run_group(log_n, x.data(), x.data(), stw)) return rc;
+        for (int64_t e = 0; e < n; ++e)
+          recv[e >> lb][p * b * b + peer_offset(f, e, lb)] = x[e];
+      }
+    for (int p = 0; p < nranks; ++p) {
+      PassPlan cols;
+      plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::Ws,
+                   PassBuf::Out);
+      if (int rc = run_plan(cols, recv[p].data(), row_out ? recv[p].data() : out[p].data(),
+                            ws[p].data()))
+        return rc;
+    }
+    if (row_out)  // peer_block_gather_kernel after a barrier
+      for (int p = 0; p < nranks; ++p)
+        for (int q = 0; q < nranks; ++q)
+          for (int64_t r = 0; r < b; ++r)
+            for (int64_t c = 0; c < b; ++c)
+              out[p][r * n + q * b + c] = recv[q][p * b * b + r * b + c];
+  } else {
+    for (int p = 0; p < nranks; ++p) {
+      PassPlan cols;
+      plan_columns(cols, log_n, lb, b, 1, n * b, inv, false, 1.0f, PassBuf::In, PassBuf::Ws,
+                   PassBuf::Out);
+      if (int rc = run_plan(cols, in[p].data(), recv[p].data(), ws[p].data())) return rc;
+    }
+    // fft_rows_gather_kernel after the barrier.
+    for (int p = 0; p < nranks; ++p)
+      for (int64_t f = 0; f < b; ++f) {
+        for (int64_t e = 0; e < n; ++e) x[e] = recv[e >> lb][p * b * b + peer_offset(f, e, lb)];
+        if (int rc = run_group(log_n, x.data(), x.data(), stw)) return rc;
+        for (int64_t e = 0; e < n; ++e) out[p][f * n + e] = epi(x[e], inv, scale);
+      }
+  }
+  for (int p = 0; p < nranks; ++p)
+    for (int64_t r = 0; r < (row_out ? b : n); ++r)
+      for (int64_t c = 0; c < (row_out ? n : b); ++c) {
+        const float2 v = out[p][r * (row_out ? n : b) + c];
+        if (row_out)
+          d[(p * b + r) * n + c] = v;
+        else
+          d[r * n + p * b + c] = v;
+      }
+  return 0;
+}
+
 int emu_fft_2d_dist_layout(float* data, int log_n, int nranks, int direction, int normalize,
                            int in_layout, int out_layout) {
   if (log_n < 2 || log_n > kMaxSinglePassLogN || nranks < 1) return -1;

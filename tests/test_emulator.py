@@ -96,3 +96,21 @@ def test_distributed_2d_transposed_layouts(emulator, oracle_mod, log_n, ranks, l
     back = layouts[::-1]
     assert emulator.emu_fft_2d_dist_layout(inv.ctypes.data, log_n, ranks, -1, 1, *back) == 0
     assert max_rel_err(inv, x) < TOL
+
+
+@pytest.mark.parametrize("log_n,ranks", [(4, 2), (6, 8), (10, 4), (11, 2), (12, 8), (12, 2)])
+@pytest.mark.parametrize("layouts", [(0, 0), (0, 1), (1, 0)])
+@pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
+def test_distributed_2d_peer_path(emulator, oracle_mod, log_n, ranks, layouts, direction,
+                                  normalize):
+    """The peer-memory path of the distributed transform (row-FFT scatter into
+    the ranks' receive slabs, column passes, row-FFT gather / block gather),
+    with the kernels' index arithmetic, against the 2D oracle."""
+    rng = np.random.default_rng(600 + log_n + ranks)
+    n = 1 << log_n
+    x = rand_c64(rng, (n, n), "normal")
+    y = x.copy()
+    assert emulator.emu_fft_2d_dist_p2p(y.ctypes.data, log_n, ranks, _dir(direction),
+                                        int(normalize), *layouts) == 0
+    ref = oracle_mod.fft_2d(x, log_n, direction, normalize, threads=8)
+    assert max_rel_err(y, ref) < TOL

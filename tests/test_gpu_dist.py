@@ -1,11 +1,20 @@
-"""Distributed 2D FFT on 2..4 GPUs (skipped with fewer than 2).
+"""Distributed 2D FFT on 2, 4 and 8 GPUs (each case skipped without enough GPUs).
 
 One process per GPU. The communicator id travels over a gloo process group;
-the data path is ferrum_fft_2d_c2c_pow2_dist (row FFTs, NCCL all-to-all,
-column FFTs, all-to-all, block gather). Each rank checks its output slab
-against the CPU oracle's 2D result (max rel err <= 1e-4), and a forward +
-inverse round trip recovers its input slab. NVLS is disabled so that a rank
-that fails cannot leave an NVLink multicast object bound.
+the data path is ferrum_fft_2d_c2c_pow2_dist_layout, run both ways: over peer
+memory (the exchange fused into the FFT kernels; the test checks that this
+path was taken) and with FERRUM_DIST_P2P=0 over NCCL send/recv. Each rank
+checks its output slab against the CPU oracle's 2D result (max rel err <=
+1e-4) for every layout pair, and forward + inverse round trips recover its
+input slab. NVLS is disabled so that a rank that fails cannot leave an NVLink
+multicast object bound.
+
+The barrier test makes one rank's device-side wait run out (its peer never
+arrives) and checks that ferrum_dist_sync reports FERRUM_ERR_TIMEOUT; the
+waiting kernel returns on its own after the context's timeout. The other rank
+learns of the failure on the host (the gloo group) between steps, with no
+kernel or collective in flight, and aborts its context instead of meeting
+the failed rank again.
 """
 
 from __future__ import annotations
@@ -32,7 +41,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cases, q):
+def _worker(rank, world, port, cases, q, p2p):
     import datetime
 
     import torch
@@ -42,6 +51,7 @@ def _worker(rank, world, port, cases, q):
         if p not in sys.path:
             sys.path.insert(0, p)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["FERRUM_DIST_P2P"] = "1" if p2p else "0"
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     try:
@@ -75,32 +85,115 @@ def _worker(rank, world, port, cases, q):
             back_c = ctx.fft_2d_tensor(cols, log_n, "inverse", True, in_layout="cols")
             rt_c = float((back_c - slab).abs().max() / slab.abs().max())
             results.append((log_n, max(err, err_c), max(rt, rt_c)))
+        path = ctx.peer_path
         ctx.close()
         dev.close()
         dist.destroy_process_group()
-        q.put((rank, "ok", results))
+        q.put((rank, "ok", (path, results)))
     except Exception as e:  # noqa: BLE001
         q.put((rank, "error", repr(e)))
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_distributed_2d_matches_oracle(world):
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
+def _spawn(target, world, *args, wait_s: float = 600):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    cases = [6, 10, 12]
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cases, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port) + args + (q,)) for r in range(world)]
     for p in procs:
         p.start()
-    out = [q.get(timeout=600) for _ in range(world)]
-    for p in procs:
-        p.join(timeout=120)
+    try:
+        out = [q.get(timeout=wait_s) for _ in range(world)]
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    return out
+
+
+def _worker_entry(rank, world, port, cases, p2p, q):
+    _worker(rank, world, port, cases, q, p2p)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("p2p", [True, False], ids=["peer", "nccl"])
+def test_distributed_2d_matches_oracle(world, p2p):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = _spawn(_worker_entry, world, [6, 10, 12], p2p)
     for rank, status, payload in out:
         assert status == "ok", f"rank {rank}: {payload}"
-        for log_n, err, rt in payload:
+        path, results = payload
+        assert path == (1 if p2p else 0), (rank, path)
+        for log_n, err, rt in results:
             assert err < 1e-4, (rank, log_n, err)
             assert rt < 1e-4, (rank, log_n, rt)
+
+
+def _barrier_worker(rank, world, port, q):
+    import datetime
+    import faulthandler
+
+    faulthandler.dump_traceback_later(100, exit=True)
+
+    import torch
+    import torch.distributed as dist
+
+    for p in (REPO, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["FERRUM_DIST_P2P"] = "1"
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        torch.cuda.set_device(rank)
+        from ferrum_gpu import capi
+        from ferrum_gpu import dist as fdist
+
+        dev = capi.DeviceHandle(rank)
+        ctx = fdist.Dist2D(dev, timeout_ms=120000)
+        slab = torch.zeros((32, 64), dtype=torch.complex64, device="cuda")
+        ctx.fft_2d_tensor(slab, 6)           # sets up the peer path, completes
+        ctx.set_timeout(1500)                 # short bound for the barrier waits
+        ok_barrier = None
+        if ctx.peer_path == 1:
+            ctx.barrier()                     # both ranks: met
+            ctx.sync()
+            ok_barrier = True
+        dist.barrier()
+        status = None
+        if rank == 0 and ctx.peer_path == 1:
+            ctx.barrier()                     # rank 1 never arrives
+            try:
+                ctx.sync()
+                status = capi.FERRUM_OK
+            except capi.FerrumError as e:
+                status = e.status
+        dist.barrier()
+        path = ctx.peer_path
+        if rank != 0:
+            ctx.abort()                       # rank 0 failed: do not meet it again
+        ctx.close()
+        dev.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok", (path, ok_barrier, status)))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", repr(e)))
+
+
+def test_peer_barrier_timeout_is_reported():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from ferrum_gpu import capi
+
+    out = dict((r, (st, pl)) for r, st, pl in _spawn(_barrier_worker, 2, wait_s=150))
+    for rank, (status, payload) in out.items():
+        assert status == "ok", f"rank {rank}: {payload}"
+    path, ok_barrier, status = out[0][1]
+    assert path == 1 and ok_barrier
+    assert status == capi.FERRUM_ERR_TIMEOUT
