@@ -165,6 +165,11 @@ def cpu_baseline_leg(target_seconds: float, log_n: int, batch: int) -> dict:
     sample = max(threads, int(target_seconds / max(per, 1e-9)))
     sample = min(sample, batch)
     dt, nbytes = time_oracle(sample, threads, log_n, seed=2)
+    # Single-threaded, as the reference's CPU path runs (crates/ferrum-gpu-fft/src/cpu.rs:101):
+    # a short sample of about a tenth of the target time.
+    per1 = calibrate_oracle(1, log_n)
+    sample1 = max(1, min(batch, int(0.1 * target_seconds / max(per1, 1e-9))))
+    dt1, nbytes1 = time_oracle(sample1, 1, log_n, seed=3)
     return {
         "value": round(nbytes / dt / 1e9, 3),
         "unit": UNIT,
@@ -173,6 +178,8 @@ def cpu_baseline_leg(target_seconds: float, log_n: int, batch: int) -> dict:
         "sample": f"{sample} of the {batch} transforms (N={1 << log_n}), forward+inverse, "
                   f"lane-parallel oracle (C restatement of crates/ferrum-gpu-fft/src/cpu.rs) "
                   f"on {threads} threads, {cpu_model()}; {dt:.1f} s",
+        "single_thread": {"value": round(nbytes1 / dt1 / 1e9, 3), "unit": UNIT, "cores": 1,
+                          "sample": f"{sample1} transforms, forward+inverse, {dt1:.1f} s"},
     }
 
 
@@ -357,8 +364,8 @@ def measure_extras(capi, dev, x, y, world, rank, barrier, max_over_ranks) -> dic
         ys = y[: rows * n]
         zs = torch.empty_like(xs)
         barrier()
-        # Forward: row slabs -> column slabs (row FFTs, one NCCL all-to-all,
-        # column FFTs); inverse: column slabs -> row slabs.
+        # Forward: row slabs -> column slabs (row FFTs, one all-to-all
+        # exchange, column FFTs); inverse: column slabs -> row slabs.
         ms_f = max_over_ranks(_time_ms(lambda: ctx.fft_2d(xs.data_ptr(), ys.data_ptr(), 14,
                                                           "forward", False, sp, "rows", "cols"),
                                        stream))
@@ -373,12 +380,17 @@ def measure_extras(capi, dev, x, y, world, rank, barrier, max_over_ranks) -> dic
         ctx.sync(sp)
         err = max_over_ranks(float((zs - xs).abs().max() / xs.abs().max()))
         barrier()
+        peer = ctx.peer_path == 1
         ctx.close()
+        slab_bytes = rows * n * 8
         out["2d_16384^2_fwd"] = {"ms": round(ms_f, 4), "inverse_ms": round(ms_i, 4),
                                  "rows_to_rows_fwd_ms": round(ms_rr, 4),
+                                 "data_path": "peer memory (exchange fused into the FFT kernels)"
+                                 if peer else "NCCL send/recv",
+                                 "nvlink_bytes_per_rank_each_way": (world - 1) * slab_bytes // world,
                                  "path": f"distributed over {world} GPUs: row slabs -> column "
-                                         f"slabs (one NCCL all-to-all, chunked and overlapped); "
-                                         f"inverse column -> row slabs",
+                                         f"slabs (one all-to-all exchange); inverse column -> "
+                                         f"row slabs",
                                  "roundtrip_max_rel_err": err}
     return out
 
@@ -527,6 +539,8 @@ def run_ours(args) -> None:
             "config": workload_config(L, B_),
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
             "transforms_per_s": round(world * args.steps * 2 * B_ / (elapsed_ms * 1e-3), 1),
+            "nominal_gflops": round(world * args.steps * 2 * 5 * n * L * B_ / (elapsed_ms * 1e-3)
+                                    / 1e9, 1),
             "roofline": {
                 "bound": "hbm",
                 "kernel": rows_kernel_name(L),
