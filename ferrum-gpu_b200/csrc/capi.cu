@@ -126,6 +126,14 @@ ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* i
       case PassKind::RowsT:
         e = launch_rows_t(d.log_n, d.conj_out, src, dst, stw, d.ra, stream);
         break;
+      case PassKind::ColsL2: {
+        ColsL2Args a = d.ca;
+        a.tw_lo = tw4_lo_table(dev, d.log_n);
+        a.tw_hi = tw4_hi_table(dev, d.log_n);
+        e = launch_cols_l2(d.log_n, d.conj_in, d.conj_out, src, dst, ws,
+                           stage_table(dev, d.cl2_l1), stage_table(dev, d.cl2_l2), a, stream);
+        break;
+      }
     }
     if (e != cudaSuccess)
       return cuda_error(e, (std::string("pass ") + std::to_string(i) + " launch").c_str());

@@ -19,6 +19,8 @@
 
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "stockham.cuh"
 
 namespace ferrum {
@@ -28,6 +30,14 @@ struct SyncBlock {
 };
 struct SyncWarp {
   __device__ __forceinline__ void operator()() const { __syncwarp(); }
+};
+// Barrier of the `count` threads (whole warps) of one thread group, on named
+// barrier `id` (1..15; 0 is __syncthreads).
+struct SyncNamed {
+  int id, count;
+  __device__ __forceinline__ void operator()() const {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+  }
 };
 
 // Per-group shared-memory stride (complex slots). `G` groups share one
@@ -166,6 +176,64 @@ struct PassCfg {
   static constexpr size_t SMEM_BYTES = G::STAGES > 1 ? (size_t)FPB * RS * sizeof(float2) : 0;
 };
 
+// One strided length-2^LOGN transform per thread group: thread t loads
+// src[(t + T*m) * in_e], runs the stages, multiplies output k = t + T*m by
+// W_M^(tw_e0 + tw_d*m) when TW, and stores dst[(t + T*m) * out_e]. With
+// LD_STREAM / ST_STREAM the data is read or written once and takes the
+// streaming (evict-first) hints; otherwise it is scratch kept in L2 between a
+// store and one later load: stores carry an L2 evict-last policy and loads an
+// evict-first one (the line is dead after it), which cut the scratch lines
+// written back to HBM.
+template <int LOGN, int LOGP, bool CONJ_IN, bool CONJ_OUT, bool TW, bool LD_STREAM, bool ST_STREAM,
+          class Sync>
+__device__ __forceinline__ void strided_unit(const float2* src, int64_t in_e, float2* dst,
+                                             int64_t out_e, bool valid, int t, float2* sm,
+                                             const float2* __restrict__ tw, uint32_t tw_e0,
+                                             uint32_t tw_d, const float2* tw_lo,
+                                             const float2* tw_hi, uint32_t tw_mask, float scale,
+                                             Sync sync) {
+  using G = Geom<LOGN, LOGP>;
+  float2 v[G::P];
+  if (valid) {
+    src += (int64_t)t * in_e;
+    const int64_t step = (int64_t)G::T * in_e;
+    uint64_t pol_first = 0;
+    if constexpr (!LD_STREAM) asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_first));
+#pragma unroll
+    for (int m = 0; m < G::P; ++m) {
+      float2 x;
+      if constexpr (LD_STREAM) {
+        x = ld_stream(src + step * m);
+      } else {
+        asm volatile("ld.global.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
+                     : "=f"(x.x), "=f"(x.y) : "l"(src + step * m), "l"(pol_first));
+      }
+      v[m] = conj_if(x, CONJ_IN);
+    }
+  } else {
+#pragma unroll
+    for (int m = 0; m < G::P; ++m) v[m] = make_float2(0.f, 0.f);
+  }
+  run_stages<LOGN, LOGP, 0>(v, sm, t, tw, sync);
+  if (valid) {
+    if constexpr (TW) apply_progression_twiddles<G::P>(v, tw_lo, tw_hi, tw_e0, tw_d, tw_mask);
+    dst += (int64_t)t * out_e;
+    const int64_t step = (int64_t)G::T * out_e;
+#pragma unroll
+    for (int m = 0; m < G::P; ++m) {
+      const float2 r = epilogue<CONJ_OUT>(v[m], scale);
+      if constexpr (ST_STREAM) {
+        st_stream(dst + step * m, r);
+      } else {
+        uint64_t pol_last;
+        asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_last));
+        asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(dst + step * m),
+                     "f"(r.x), "f"(r.y), "l"(pol_last) : "memory");
+      }
+    }
+  }
+}
+
 template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW>
 __global__ void __launch_bounds__(PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS,
                                   MinBlocks<PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS, LOGP>::value)
@@ -179,33 +247,124 @@ fft_pass_kernel(const float2* in, float2* out, const float2* __restrict__ tw, Pa
   const bool valid = f < a.nfft;
   int64_t o, j, c;
   pass_index(f, a.log_w, a.log_j, o, j, c);
-
-  float2 v[G::P];
-  if (valid) {
-    const float2* src = in + o * a.in_o + j * a.in_j + c + (int64_t)t * a.in_e;
-    const int64_t step = (int64_t)G::T * a.in_e;
-#pragma unroll
-    for (int m = 0; m < G::P; ++m) v[m] = conj_if(ld_stream(src + step * m), CONJ_IN);
-  } else {
-#pragma unroll
-    for (int m = 0; m < G::P; ++m) v[m] = make_float2(0.f, 0.f);
-  }
+  // Output k = t + T*m takes W_M^(tb + ts*k): a progression in m.
+  const uint32_t tb = TW ? pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj) : 0u;
+  const uint32_t ts = TW ? pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj) : 0u;
+  const uint32_t mask = TW ? (1u << a.log_m) - 1u : 0u;
+  float2* sm = smem + (C::SMEM_BYTES ? cl * C::RS : 0);
+  const float2* src = in + o * a.in_o + j * a.in_j + c;
+  float2* dst = out + o * a.out_o + j * a.out_j + c;
   if constexpr (FPB == 1 && G::T <= 32)
-    run_stages<LOGN, LOGP, 0>(v, smem + (C::SMEM_BYTES ? cl * C::RS : 0), t, tw, SyncWarp{});
+    strided_unit<LOGN, LOGP, CONJ_IN, CONJ_OUT, TW, true, true>(
+        src, a.in_e, dst, a.out_e, valid, t, sm, tw, tb + ts * (uint32_t)t, ts * (uint32_t)G::T,
+        a.tw_lo, a.tw_hi, mask, a.scale, SyncWarp{});
   else
-    run_stages<LOGN, LOGP, 0>(v, smem + (C::SMEM_BYTES ? cl * C::RS : 0), t, tw, SyncBlock{});
-  if (valid) {
-    float2* dst = out + o * a.out_o + j * a.out_j + c + (int64_t)t * a.out_e;
-    const int64_t step = (int64_t)G::T * a.out_e;
-    if constexpr (TW) {
-      // Output k = t + T*m takes W_M^(tb + ts*k): a progression in m.
-      const uint32_t tb = pass_tw_base((uint32_t)c, (uint32_t)j, a.tcj);
-      const uint32_t ts = pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj);
-      apply_progression_twiddles<G::P>(v, a.tw_lo, a.tw_hi, tb + ts * (uint32_t)t,
-                                       ts * (uint32_t)G::T, (1u << a.log_m) - 1u);
+    strided_unit<LOGN, LOGP, CONJ_IN, CONJ_OUT, TW, true, true>(
+        src, a.in_e, dst, a.out_e, valid, t, sm, tw, tb + ts * (uint32_t)t, ts * (uint32_t)G::T,
+        a.tw_lo, a.tw_hi, mask, a.scale, SyncBlock{});
+}
+
+// ----------------------------------------------------------------------------
+// Column FFTs of length N = 2^(L1 + L2) as both sub-passes in one persistent
+// kernel (N = A*B, A = 2^L2, B = 2^L1, column element n = a + A*b):
+//   sub-pass 1, unit a < A: DFT over b of rows a + A*b, times W_N^(a*kb),
+//               stored to rows a + A*kb of the CTA's scratch slot;
+//   sub-pass 2, unit kb < B: DFT over a of slot rows A*kb + a, stored to
+//               output row kb + B*ka.
+// A CTA takes tiles of W adjacent columns of one image (all N rows) in turn;
+// its slot (N x W values, row pitch W) is rewritten for every tile, so the
+// slots of all CTAs (a few tens of MiB) stay in L2 and HBM sees one read and
+// one write per element instead of two of each for two separate passes.
+// The input is read with evict-first hints, the slot with normal ones. A unit
+// (W columns x T threads) is one warp or a few whole warps, and runs its
+// rounds on its own with a warp barrier or a named barrier of its warps, so
+// the units of a CTA overlap each other's memory latency; only the two
+// sub-pass boundaries of a tile are block-wide barriers.
+struct ColsL2Args {
+  int64_t tiles;           // images * (width / W)
+  int log_tiles_per_img;   // log2(width / W)
+  int64_t img_stride;      // input and output image stride (elements)
+  int64_t ld;              // input and output row pitch (elements)
+  const float2* tw_lo;     // two-level W_N tables
+  const float2* tw_hi;
+  float scale;
+};
+
+template <int L1, int L2, int W, int THREADS>
+struct ColsL2Cfg {
+  static constexpr int LP1 = plan_log_p(L1), LP2 = plan_log_p(L2);
+  using G1 = Geom<L1, LP1>;
+  using G2 = Geom<L2, LP2>;
+  static constexpr int U1 = THREADS / (W * G1::T);  // sub-pass-1 units per round
+  static constexpr int U2 = THREADS / (W * G2::T);
+  static constexpr int A = 1 << L2, B = 1 << L1;
+  static_assert(U1 >= 1 && U2 >= 1 && THREADS % (W * G1::T) == 0 && THREADS % (W * G2::T) == 0,
+                "a round must be whole units");
+  static_assert(A % U1 == 0 && B % U2 == 0, "whole rounds per sub-pass");
+  static constexpr int RS1 = RegionStride<L1, LP1, (W < 16 ? W : 16)>::value;
+  static constexpr int RS2 = RegionStride<L2, LP2, (W < 16 ? W : 16)>::value;
+  static constexpr size_t SM1 = G1::STAGES > 1 ? (size_t)U1 * W * RS1 : 0;
+  static constexpr size_t SM2 = G2::STAGES > 1 ? (size_t)U2 * W * RS2 : 0;
+  static constexpr size_t SMEM_BYTES = (SM1 > SM2 ? SM1 : SM2) * sizeof(float2);
+  static constexpr int64_t SLOT = (int64_t)W << (L1 + L2);  // complex values per CTA
+};
+
+template <int L1, int L2, int W, int THREADS, int MINB, bool CONJ_IN, bool CONJ_OUT>
+__global__ void __launch_bounds__(THREADS, MINB)
+fft_cols_l2_kernel(const float2* in, float2* out, float2* ws, const float2* __restrict__ tw1,
+                   const float2* __restrict__ tw2, ColsL2Args a) {
+  using C = ColsL2Cfg<L1, L2, W, THREADS>;
+  extern __shared__ float2 smem[];
+  constexpr int A = C::A, B = C::B;
+  constexpr uint32_t kMask = (1u << (L1 + L2)) - 1u;
+  constexpr int kUnit1 = W * C::G1::T, kUnit2 = W * C::G2::T;
+  static_assert(kUnit1 <= 32 || (kUnit1 % 32 == 0 && C::U1 <= 15), "unit barriers");
+  static_assert(kUnit2 <= 32 || (kUnit2 % 32 == 0 && C::U2 <= 15), "unit barriers");
+  float2* slot = ws + (int64_t)blockIdx.x * C::SLOT;
+  const int cl = threadIdx.x % W;
+  const int64_t tile_mask = ((int64_t)1 << a.log_tiles_per_img) - 1;
+  for (int64_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
+    const int64_t base = (tile >> a.log_tiles_per_img) * a.img_stride + (tile & tile_mask) * W + cl;
+    {
+      const int t1 = (threadIdx.x / W) % C::G1::T, u1 = threadIdx.x / (W * C::G1::T);
+      float2* sm1 = smem + (u1 * W + cl) * C::RS1;
+      using Sync1 = typename std::conditional<(kUnit1 <= 32), SyncWarp, SyncNamed>::type;
+      Sync1 sync1;
+      if constexpr (kUnit1 > 32) sync1 = SyncNamed{1 + u1, kUnit1};
+#pragma unroll 1
+      for (int r = 0; r < A / C::U1; ++r) {
+        const int j = r * C::U1 + u1;  // a
+        // The stage twiddles depend on the thread only; an opaque table
+        // pointer keeps them from being hoisted out of the loop and held in
+        // registers across rounds (which spilled at 64 registers).
+        const float2* twr = tw1;
+        asm volatile("" : "+l"(twr));
+        strided_unit<L1, C::LP1, CONJ_IN, false, true, true, false>(
+            in + base + j * a.ld, (int64_t)A * a.ld, slot + j * W + cl, (int64_t)A * W, true, t1,
+            sm1, twr, (uint32_t)j * (uint32_t)t1, (uint32_t)j * (uint32_t)C::G1::T, a.tw_lo,
+            a.tw_hi, kMask, 1.0f, sync1);
+        sync1();  // the next round's first exchange reuses the unit's shared region
+      }
     }
-#pragma unroll
-    for (int m = 0; m < G::P; ++m) st_stream(dst + step * m, epilogue<CONJ_OUT>(v[m], a.scale));
+    __syncthreads();  // the tile's slot is complete
+    {
+      const int t2 = (threadIdx.x / W) % C::G2::T, u2 = threadIdx.x / (W * C::G2::T);
+      float2* sm2 = smem + (u2 * W + cl) * C::RS2;
+      using Sync2 = typename std::conditional<(kUnit2 <= 32), SyncWarp, SyncNamed>::type;
+      Sync2 sync2;
+      if constexpr (kUnit2 > 32) sync2 = SyncNamed{1 + u2, kUnit2};
+#pragma unroll 1
+      for (int r = 0; r < B / C::U2; ++r) {
+        const int j = r * C::U2 + u2;  // kb
+        const float2* twr = tw2;
+        asm volatile("" : "+l"(twr));
+        strided_unit<L2, C::LP2, false, CONJ_OUT, false, false, true>(
+            slot + (int64_t)A * j * W + cl, (int64_t)W, out + base + j * a.ld, (int64_t)B * a.ld,
+            true, t2, sm2, twr, 0u, 0u, nullptr, nullptr, 0u, a.scale, sync2);
+        sync2();
+      }
+    }
+    __syncthreads();  // every read of the slot is done before the next tile rewrites it
   }
 }
 

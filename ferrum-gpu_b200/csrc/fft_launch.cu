@@ -150,6 +150,33 @@ cudaError_t pass_impl(const float2* in, float2* out, const float2* tw, const Pas
   return cudaGetLastError();
 }
 
+template <int L1, int L2, int W, int THREADS, int MINB, bool CI, bool CO>
+cudaError_t cols_l2_impl(const float2* in, float2* out, float2* ws, const float2* tw1,
+                         const float2* tw2, const ColsL2Args& a, int64_t slots, cudaStream_t s) {
+  using C = ColsL2Cfg<L1, L2, W, THREADS>;
+  auto k = fft_cols_l2_kernel<L1, L2, W, THREADS, MINB, CI, CO>;
+  static std::atomic<uint64_t> smem_done{0};
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
+  if (e != cudaSuccess) return e;
+  const int64_t grid = a.tiles < slots ? a.tiles : slots;
+  if (grid < 1) return cudaSuccess;
+  k<<<(unsigned)grid, THREADS, C::SMEM_BYTES, s>>>(in, out, ws, tw1, tw2, a);
+  return cudaGetLastError();
+}
+
+template <int L1, int L2, int W, int THREADS, int MINB>
+cudaError_t cols_l2_dispatch(bool ci, bool co, const float2* in, float2* out, float2* ws,
+                             const float2* tw1, const float2* tw2, const ColsL2Args& a,
+                             int64_t slots, cudaStream_t s) {
+  if (ci && co)
+    return cols_l2_impl<L1, L2, W, THREADS, MINB, true, true>(in, out, ws, tw1, tw2, a, slots, s);
+  if (ci)
+    return cols_l2_impl<L1, L2, W, THREADS, MINB, true, false>(in, out, ws, tw1, tw2, a, slots, s);
+  if (co)
+    return cols_l2_impl<L1, L2, W, THREADS, MINB, false, true>(in, out, ws, tw1, tw2, a, slots, s);
+  return cols_l2_impl<L1, L2, W, THREADS, MINB, false, false>(in, out, ws, tw1, tw2, a, slots, s);
+}
+
 template <int LOGN, bool CO>
 cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const RowsTArgs& a,
                         cudaStream_t s) {
@@ -363,6 +390,24 @@ cudaError_t launch_pass(int log_n, bool conj_in, bool conj_out, bool tw, const f
     return pass_dispatch<L>(conj_in, conj_out, tw, in, out, stage_tw, args, stream);
     FERRUM_CASE_2_14(X)
 #undef X
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_cols_l2(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
+                           float2* ws, const float2* tw1, const float2* tw2, const ColsL2Args& a,
+                           cudaStream_t stream) {
+  if (ws == nullptr || cols_l2_width(log_n) == 0) return cudaErrorInvalidValue;
+  const int64_t slots = cols_l2_slots(log_n);
+  switch (log_n) {
+#define FERRUM_COLS_L2(L)                                                                  \
+  case L:                                                                                  \
+    return cols_l2_dispatch<L - L / 2, L / 2, cols_l2_width(L), cols_l2_threads(L),        \
+                            cols_l2_ctas_per_sm(L)>(conj_in, conj_out, in, out, ws, tw1, tw2, a, \
+                                                    slots, stream);
+    FERRUM_COLS_L2(12)
+#undef FERRUM_COLS_L2
     default:
       return cudaErrorInvalidValue;
   }

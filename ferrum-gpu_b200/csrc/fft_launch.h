@@ -8,6 +8,7 @@ namespace ferrum {
 
 struct PassArgs;
 struct RowsTArgs;
+struct ColsL2Args;
 struct PeerPtrs;
 struct PeerFlags;
 
@@ -36,6 +37,14 @@ cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, 
 cudaError_t launch_pass(int log_n, bool conj_in, bool conj_out, bool tw, const float2* in,
                         float2* out, const float2* stage_tw, const PassArgs& args,
                         cudaStream_t stream);
+
+// Both column sub-passes of length 2^log_n (the lengths cols_l2_width() in
+// passes.h enables) in one persistent kernel; `ws` holds
+// cols_l2_slots(log_n) scratch slots, tw1 / tw2 are the stage tables of the
+// sub-pass lengths 2^(log_n - log_n/2) and 2^(log_n/2).
+cudaError_t launch_cols_l2(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
+                           float2* ws, const float2* tw1, const float2* tw2, const ColsL2Args& args,
+                           cudaStream_t stream);
 
 // Rows of length 2^log_n (4 <= log_n <= 14) stored transposed.
 cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* out,

@@ -16,7 +16,9 @@
 //     reads 32-byte row segments, still near full DRAM efficiency on B200).
 //   * 2D, N >= 4096: columns first as two sub-passes (N = A*B, row a + A*b:
 //     DFT over b times W_N^(a*kb), then DFT over a stored to row kb + B*ka),
-//     then the row pass, which also applies the inverse's conjugate and scale.
+//     run by one persistent kernel that keeps the intermediate of each tile of
+//     columns in an L2-resident scratch slot (fft_cols_l2_kernel), then the
+//     row pass in place, which also applies the inverse's conjugate and scale.
 // The index identities are the Cooley-Tukey splits; the reference's CPU
 // Stockham (crates/ferrum-gpu-fft/src/cpu.rs) defines the results they must
 // reproduce.
@@ -29,7 +31,7 @@
 
 namespace ferrum {
 
-enum class PassKind : int { Rows = 0, Pass = 1, RowsT = 2 };
+enum class PassKind : int { Rows = 0, Pass = 1, RowsT = 2, ColsL2 = 3 };
 enum class PassBuf : int { In = 0, Out = 1, Ws = 2 };
 
 struct PassDesc {
@@ -45,6 +47,10 @@ struct PassDesc {
   // Pass / RowsT (twiddle tables are filled in by the executor from log_m)
   PassArgs pa;
   RowsTArgs ra;
+  // ColsL2: sub-pass lengths 2^l1 (first) and 2^l2 (second), log_n = l1 + l2;
+  // the executor fills the twiddle tables. Scratch slots live in PassBuf::Ws.
+  int cl2_l1, cl2_l2;
+  ColsL2Args ca;
 };
 
 struct PassPlan {
@@ -113,6 +119,47 @@ inline PassArgs pass_args(int64_t nfft, int log_w, int log_j, int64_t in_o, int6
   a.out_e = out_e;
   a.scale = 1.0f;
   return a;
+}
+
+// The fused column kernel (fft_cols_l2_kernel) per column length: columns per
+// tile W (0 = the length keeps two separate sub-passes), threads and resident
+// CTAs per SM, and scratch slots (one per resident CTA on a 148-SM B200).
+// Measured on 2D N x N transforms (2 GiB): the sub-pass loop needs ~127
+// registers (at 64 it spilled); one 512-thread CTA per SM with W = 8 at
+// N = 4096 (a 37 MiB slot set) beat the separate sub-passes (1.88 vs 2.10 ms
+// for 4096^2 x 16), while a 74 MiB slot set (two CTAs per SM, or W = 8 at
+// N = 8192) lost to them: the L2 keeps the slots only well below its 126 MB.
+// 32-byte row segments (W = 4) at N >= 8192 were worse still, so N >= 8192
+// keeps the separate sub-passes.
+constexpr int cols_l2_width(int log_n) { return log_n == 12 ? 8 : 0; }
+constexpr int cols_l2_threads(int) { return 512; }
+constexpr int cols_l2_ctas_per_sm(int) { return 1; }
+constexpr int cols_l2_slots(int log_n) { return 148 * cols_l2_ctas_per_sm(log_n); }
+
+inline PassDesc make_cols_l2(int log_n, int log_width, int64_t ld, int64_t images,
+                             int64_t img_stride, bool ci, bool co, float scale, PassBuf src,
+                             PassBuf dst) {
+  PassDesc d{};
+  d.kind = PassKind::ColsL2;
+  d.log_n = log_n;
+  d.conj_in = ci;
+  d.conj_out = co;
+  d.src = src;
+  d.dst = dst;
+  d.cl2_l2 = log_n / 2;
+  d.cl2_l1 = log_n - d.cl2_l2;
+  int lw = 0;
+  while ((1 << lw) < cols_l2_width(log_n)) ++lw;
+  d.ca.tiles = images << (log_width - lw);
+  d.ca.log_tiles_per_img = log_width - lw;
+  d.ca.img_stride = img_stride;
+  d.ca.ld = ld;
+  d.ca.scale = scale;
+  return d;
+}
+
+inline int64_t cols_l2_ws_elems(int log_n) {
+  return (int64_t)cols_l2_slots(log_n) * cols_l2_width(log_n) * ((int64_t)1 << log_n);
 }
 
 // Passes of a multi-pass 1D transform.
@@ -187,6 +234,15 @@ inline void plan_columns(PassPlan& pl, int log_n, int log_width, int64_t ld, int
                          int64_t img_stride, bool ci, bool co, float scale, PassBuf src,
                          PassBuf mid, PassBuf dst) {
   const int64_t width = (int64_t)1 << log_width;
+  // Both sub-passes in one kernel when the plan has a workspace for the slots
+  // (mid == Ws) and the columns split into whole tiles.
+  if (log_n > kMaxOnePassColumnLogN && mid == PassBuf::Ws && cols_l2_width(log_n) > 0 &&
+      width >= cols_l2_width(log_n)) {
+    pl.p[pl.count++] = make_cols_l2(log_n, log_width, ld, images, img_stride, ci, co, scale, src,
+                                    dst);
+    if (pl.ws_elems < cols_l2_ws_elems(log_n)) pl.ws_elems = cols_l2_ws_elems(log_n);
+    return;
+  }
   if (log_n <= kMaxOnePassColumnLogN) {
     PassArgs a = pass_args(images * width, log_width, 0, img_stride, 0, ld, img_stride, 0, ld);
     a.scale = scale;
@@ -217,6 +273,13 @@ inline PassPlan plan_2d(int log_n, int64_t batch, bool inv, bool normalize) {
     pl.p[pl.count++] = make_rows(log_n, batch * n, inv, false, 1.0f, PassBuf::In, PassBuf::Out);
     plan_columns(pl, log_n, log_n, n, batch, n * n, false, inv, scale, PassBuf::Out, PassBuf::Out,
                  PassBuf::Out);
+    return pl;
+  }
+  if (cols_l2_width(log_n) > 0) {
+    // Fused column kernel (slots in the workspace), then rows in place.
+    plan_columns(pl, log_n, log_n, n, batch, n * n, inv, false, 1.0f, PassBuf::In, PassBuf::Ws,
+                 PassBuf::Out);
+    pl.p[pl.count++] = make_rows(log_n, batch * n, false, inv, scale, PassBuf::Out, PassBuf::Out);
     return pl;
   }
   pl.ws_elems = batch * n * n;

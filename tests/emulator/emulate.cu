@@ -14,6 +14,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "../../ferrum-gpu_b200/csrc/dist_steps.h"
@@ -140,9 +141,49 @@ float2 epi(float2 v, bool conj_out, float scale) {
   return conj_out ? make_float2(v.x * scale, -v.y * scale) : v;
 }
 
+// fft_cols_l2_kernel: per tile of W columns, sub-pass 1 (units a < A) into
+// the tile's scratch slot (row pitch W), then sub-pass 2 (units kb < B) from
+// the slot to the output. The GPU grid is min(tiles, slots) CTAs and CTA c
+// takes tiles c, c + grid, ... with slot c, so tile t uses slot t mod grid;
+// each tile rewrites its slot before reading it.
+int run_cols_l2(const PassDesc& d, const float2* src, float2* dst, float2* ws) {
+  if (ws == nullptr) return -70;
+  const Tables& tab = tables();
+  const int l1 = d.cl2_l1, l2 = d.cl2_l2, w = cols_l2_width(d.log_n);
+  if (l1 + l2 != d.log_n || w == 0) return -71;
+  const int64_t A = (int64_t)1 << l2, B = (int64_t)1 << l1, n = A * B;
+  const uint32_t mask = (uint32_t)(n - 1);
+  const ColsL2Args& a = d.ca;
+  const int64_t grid = a.tiles < cols_l2_slots(d.log_n) ? a.tiles : cols_l2_slots(d.log_n);
+  std::vector<float2> x(n);
+  for (int64_t tile = 0; tile < a.tiles; ++tile) {
+    const int64_t tpi = (int64_t)1 << a.log_tiles_per_img;
+    const int64_t base = (tile / tpi) * a.img_stride + (tile % tpi) * w;
+    float2* slot = ws + (tile % grid) * (int64_t)w * n;
+    for (int64_t j = 0; j < A; ++j)
+      for (int cl = 0; cl < w; ++cl) {
+        for (int64_t e = 0; e < B; ++e)
+          x[e] = conj_if(src[base + cl + (j + A * e) * a.ld], d.conj_in);
+        if (int rc = run_group(l1, x.data(), x.data(), tab.stage[l1].data())) return rc;
+        if (int rc = apply_pass_twiddles(l1, x.data(), tab.lo[d.log_n].data(),
+                                         tab.hi[d.log_n].data(), 0u, (uint32_t)j, mask))
+          return rc;
+        for (int64_t k = 0; k < B; ++k) slot[(j + A * k) * w + cl] = x[k];
+      }
+    for (int64_t j = 0; j < B; ++j)
+      for (int cl = 0; cl < w; ++cl) {
+        for (int64_t e = 0; e < A; ++e) x[e] = slot[(A * j + e) * w + cl];
+        if (int rc = run_group(l2, x.data(), x.data(), tab.stage[l2].data())) return rc;
+        for (int64_t k = 0; k < A; ++k)
+          dst[base + cl + (j + B * k) * a.ld] = epi(x[k], d.conj_out, a.scale);
+      }
+  }
+  return 0;
+}
+
 // One pass of a plan, FFT by FFT (each touches disjoint elements, so in-place
 // passes behave as on the GPU).
-int run_pass(const PassDesc& d, const float2* src, float2* dst) {
+int run_pass(const PassDesc& d, const float2* src, float2* dst, float2* ws) {
   const Tables& tab = tables();
   const int64_t n = (int64_t)1 << d.log_n;
   const float2* stw = tab.stage[d.log_n].data();
@@ -185,6 +226,8 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst) {
       }
       return 0;
     }
+    case PassKind::ColsL2:
+      return run_cols_l2(d, src, dst, ws);
     case PassKind::RowsT: {
       const RowsTArgs& a = d.ra;
       if (d.conj_in || d.log_n < 4) return -61;  // fft_rows_t_kernel: no conj_in, 4 <= log_n <= 14
@@ -205,7 +248,7 @@ int run_plan(const PassPlan& pl, const float2* in, float2* out, float2* ws) {
   float2* bufs[3] = {const_cast<float2*>(in), out, ws};
   for (int i = 0; i < pl.count; ++i) {
     const PassDesc& d = pl.p[i];
-    if (int rc = run_pass(d, bufs[(int)d.src], bufs[(int)d.dst])) return rc;
+    if (int rc = run_pass(d, bufs[(int)d.src], bufs[(int)d.dst], ws)) return rc;
   }
   return 0;
 }
@@ -259,7 +302,7 @@ int emu_fft_2d_dist_p2p(float* data, int log_n, int nranks, int direction, int n
   const size_t slab = (size_t)(b * n);
   std::vector<std::vector<float2>> in(nranks, std::vector<float2>(slab)),
       out(nranks, std::vector<float2>(slab)), recv(nranks, std::vector<float2>(slab)),
-      ws(nranks, std::vector<float2>(slab));
+      ws(nranks, std::vector<float2>(std::max<size_t>(slab, (size_t)cols_l2_ws_elems(log_n))));
   for (int p = 0; p < nranks; ++p)
     for (int64_t r = 0; r < (row_in ? b : n); ++r)
       for (int64_t c = 0; c < (row_in ? n : b); ++c)
@@ -358,7 +401,7 @@ int emu_fft_2d_dist_layout(float* data, int log_n, int nranks, int direction, in
       dist_chunk(b, chunks, c, r0, r1);
       for (int p = 0; p < nranks; ++p) {
         PassDesc rows = make_rows(log_n, r1 - r0, inv, false, 1.0f, PassBuf::In, PassBuf::Out, lb, b);
-        if (int rc = run_pass(rows, in[p].data() + r0 * n, wa[p].data() + r0 * b)) return rc;
+        if (int rc = run_pass(rows, in[p].data() + r0 * n, wa[p].data() + r0 * b, nullptr)) return rc;
       }
       exchange(wa, wb, r0, r1);
     }
@@ -390,7 +433,7 @@ int emu_fft_2d_dist_layout(float* data, int log_n, int nranks, int direction, in
       for (int p = 0; p < nranks; ++p) {
         gather(wa[p].data() + r0 * b, out[p].data() + r0 * n, r1 - r0);
         PassDesc rows = make_rows(log_n, r1 - r0, false, inv, scale, PassBuf::In, PassBuf::Out);
-        if (int rc = run_pass(rows, out[p].data() + r0 * n, out[p].data() + r0 * n)) return rc;
+        if (int rc = run_pass(rows, out[p].data() + r0 * n, out[p].data() + r0 * n, nullptr)) return rc;
       }
     }
   }

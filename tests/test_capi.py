@@ -52,7 +52,10 @@ def test_workspace_and_launch_counts(capi):
     # 2D up to 1024^2: row pass + one column pass in place; from 2048^2 the
     # columns run as two sub-passes through an image-sized workspace.
     assert capi.workspace_bytes(10, 16, 2) == 0
-    assert capi.workspace_bytes(12, 16, 2) == 16 * (1 << 24) * 8
+    # 2D N >= 4096: the fused column kernel's L2 scratch slots (slots x W x N)
+    assert capi.workspace_bytes(12, 16, 2) == 148 * 8 * 4096 * 8
+    assert capi.workspace_bytes(13, 4, 2) == 4 * (1 << 26) * 8   # separate sub-passes
+    assert capi.workspace_bytes(14, 1, 2) == (1 << 28) * 8   # separate sub-passes
     assert capi.launch_count(10, 256, 1) == 1
     assert capi.launch_count(14, 1, 1) == 1
     assert capi.launch_count(15, 1, 1) == 2
@@ -62,7 +65,8 @@ def test_workspace_and_launch_counts(capi):
     assert capi.launch_count(10, 16, 2) == 2
     assert capi.launch_count(11, 64, 2) == 2
     assert capi.workspace_bytes(11, 64, 2) == 0
-    assert capi.launch_count(12, 16, 2) == 3
+    assert capi.launch_count(12, 16, 2) == 2
+    assert capi.launch_count(14, 1, 2) == 3
 
 
 @pytest.mark.parametrize("log_n,batch,kind", [(1, 1, 1), (27, 1, 1), (10, 0, 1), (15, 1, 2),
