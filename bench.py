@@ -44,6 +44,7 @@ sys.path.insert(0, os.path.join(REPO, "ferrum-gpu_b200"))
 sys.path.insert(0, REPO)
 
 METRIC = "batched 1D C2C FFT HBM GB/s"
+METRIC_2D = "batched 2D C2C FFT HBM GB/s"
 UNIT = "GB/s"
 LOG_N = 12
 BATCH = 65536
@@ -67,25 +68,41 @@ def parse_args():
                     help="skip the secondary measurements (other configs, 2D 16384^2)")
     ap.add_argument("--log-n", type=int, default=LOG_N, choices=range(2, 15),
                     help="log2 of the transform length (default 12: the headline N=4096)")
+    ap.add_argument("--kind", choices=["1d", "2d"], default="1d",
+                    help="2d: the step is a forward + inverse 2D transform of --batch N x N "
+                         "images (the 2D config); GB/s count 2 passes per transform")
     ap.add_argument("--batch", type=int, default=None,
                     help="transforms per GPU (default 2 GiB / N; smaller only for profiling)")
     args = ap.parse_args()
     if args.batch is None:
-        args.batch = TOTAL_ELEMS >> args.log_n
+        args.batch = TOTAL_ELEMS >> (args.log_n * (2 if args.kind == "2d" else 1))
     return args
 
 
-def workload_config(log_n: int, batch: int) -> dict:
-    mib = (batch << log_n) * 8 / 2**20
+def elems_per_item(log_n: int, kind: str) -> int:
+    return 1 << (log_n * (2 if kind == "2d" else 1))
+
+
+def passes_counted(kind: str) -> int:
+    """Passes the metric counts per transform: 1 (single-pass 1D) or 2 (2D)."""
+    return 2 if kind == "2d" else 1
+
+
+def workload_config(log_n: int, batch: int, kind: str = "1d") -> dict:
+    mib = batch * elems_per_item(log_n, kind) * 8 / 2**20
+    n = 1 << log_n
+    what = (f"batched 1D C2C forward+inverse(1/N), N={n}, batch={batch} per GPU"
+            if kind == "1d" else
+            f"batched 2D C2C forward+inverse(1/N^2), {n}x{n}, {batch} images per GPU")
     return {
-        "workload": f"batched 1D C2C forward+inverse(1/N), N={1 << log_n}, batch={batch} per GPU "
-                    f"({mib / 1024:g} GiB complex64), one step = 2 passes",
-        "n": 1 << log_n,
+        "workload": f"{what} ({mib / 1024:g} GiB complex64), one step = forward + inverse",
+        "n": n,
         "batch_per_gpu": batch,
         "inputs": "re/im i.i.d. uniform[-1,1), seeded",
         "l2": (f"no flush: every buffer is {mib:g} MiB > 126 MB L2" if mib > 126 else
                f"L2-resident: buffers of {mib:g} MiB fit the 126 MB L2"),
-        "bytes_counted": "16 B per complex element per pass",
+        "bytes_counted": f"16 B per complex element per pass, {passes_counted(kind)} pass(es) "
+                         f"per transform",
     }
 
 
@@ -134,48 +151,53 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def time_oracle(transforms: int, threads: int, log_n: int, seed: int = 0):
-    """Forward + inverse(1/N) of `transforms` lanes with the oracle; returns
-    (seconds, bytes counted)."""
+def time_oracle(transforms: int, threads: int, log_n: int, seed: int = 0, kind: str = "1d"):
+    """Forward + inverse (normalized) of `transforms` lanes (1D) or images (2D)
+    with the oracle; returns (seconds, bytes counted)."""
     import numpy as np
 
     import oracle
 
     rng = np.random.default_rng(seed)
     n = 1 << log_n
-    x = (rng.uniform(-1, 1, transforms * n) + 1j * rng.uniform(-1, 1, transforms * n)).astype(
-        np.complex64)
+    e = transforms * elems_per_item(log_n, kind)
+    x = (rng.uniform(-1, 1, e) + 1j * rng.uniform(-1, 1, e)).astype(np.complex64)
     t0 = time.perf_counter()
-    y = oracle.fft_1d(x, log_n, "forward", False, threads=threads)
-    oracle.fft_1d(y, log_n, "inverse", True, threads=threads)
+    if kind == "1d":
+        y = oracle.fft_1d(x, log_n, "forward", False, threads=threads)
+        oracle.fft_1d(y, log_n, "inverse", True, threads=threads)
+    else:
+        x = x.reshape(transforms, n, n)
+        y = oracle.fft_2d(x, log_n, "forward", False, threads=threads)
+        oracle.fft_2d(y, log_n, "inverse", True, threads=threads)
     dt = time.perf_counter() - t0
-    return dt, 2 * BYTES_PER_ELEM_PASS * n * transforms
+    return dt, 2 * BYTES_PER_ELEM_PASS * passes_counted(kind) * e
 
 
-def calibrate_oracle(threads: int, log_n: int) -> float:
+def calibrate_oracle(threads: int, log_n: int, kind: str = "1d") -> float:
     """Seconds per transform (fwd + inv) of the oracle on `threads` threads."""
-    probe = max(threads * 4, 64)
-    dt, _ = time_oracle(probe, threads, log_n, seed=1)
+    probe = max(threads * 4, 64) if kind == "1d" else 1
+    dt, _ = time_oracle(probe, threads, log_n, seed=1, kind=kind)
     return dt / probe
 
 
-def cpu_baseline_leg(target_seconds: float, log_n: int, batch: int) -> dict:
+def cpu_baseline_leg(target_seconds: float, log_n: int, batch: int, kind: str = "1d") -> dict:
     threads = host_cores()
-    per = calibrate_oracle(threads, log_n)
-    sample = max(threads, int(target_seconds / max(per, 1e-9)))
+    per = calibrate_oracle(threads, log_n, kind)
+    sample = max(threads if kind == "1d" else 1, int(target_seconds / max(per, 1e-9)))
     sample = min(sample, batch)
-    dt, nbytes = time_oracle(sample, threads, log_n, seed=2)
+    dt, nbytes = time_oracle(sample, threads, log_n, seed=2, kind=kind)
     # Single-threaded, as the reference's CPU path runs (crates/ferrum-gpu-fft/src/cpu.rs:101):
     # a short sample of about a tenth of the target time.
-    per1 = calibrate_oracle(1, log_n)
+    per1 = calibrate_oracle(1, log_n, kind) if kind == "1d" else per * threads
     sample1 = max(1, min(batch, int(0.1 * target_seconds / max(per1, 1e-9))))
-    dt1, nbytes1 = time_oracle(sample1, 1, log_n, seed=3)
+    dt1, nbytes1 = time_oracle(sample1, 1, log_n, seed=3, kind=kind)
     return {
         "value": round(nbytes / dt / 1e9, 3),
         "unit": UNIT,
         "cores": threads,
         "kind": "port",
-        "sample": f"{sample} of the {batch} transforms (N={1 << log_n}), forward+inverse, "
+        "sample": f"{sample} of the {batch} {kind} transforms (N={1 << log_n}), forward+inverse, "
                   f"lane-parallel oracle (C restatement of crates/ferrum-gpu-fft/src/cpu.rs) "
                   f"on {threads} threads, {cpu_model()}; {dt:.1f} s",
         "single_thread": {"value": round(nbytes1 / dt1 / 1e9, 3), "unit": UNIT, "cores": 1,
@@ -189,25 +211,26 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     threads = host_cores()
-    per = calibrate_oracle(threads, args.log_n)
+    per = calibrate_oracle(threads, args.log_n, args.kind)
     budget = 90.0
     sample = int(budget / max(per, 1e-9) / max(1, args.steps + args.warmup))
-    sample = max(threads, min(sample, args.batch))
+    sample = max(threads if args.kind == "1d" else 1, min(sample, args.batch))
     for w in range(args.warmup):
-        time_oracle(sample, threads, args.log_n, seed=100 + w)
+        time_oracle(sample, threads, args.log_n, seed=100 + w, kind=args.kind)
     total_t = 0.0
     total_b = 0
     for k in range(args.steps):
-        dt, nb = time_oracle(sample, threads, args.log_n, seed=200 + k)
+        dt, nb = time_oracle(sample, threads, args.log_n, seed=200 + k, kind=args.kind)
         total_t += dt
         total_b += nb
     value = total_b / total_t / 1e9
-    sample_desc = (f"{sample} of the {args.batch} transforms per step (N={1 << args.log_n}), "
+    sample_desc = (f"{sample} of the {args.batch} {args.kind} transforms per step "
+                   f"(N={1 << args.log_n}), "
                    f"forward+inverse(1/N), lane-parallel oracle port of "
                    f"crates/ferrum-gpu-fft/src/cpu.rs on {threads} threads, {cpu_model()}")
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": METRIC if args.kind == "1d" else METRIC_2D,
         "value": round(value, 3),
         "unit": UNIT,
         "n_gpus": world,
@@ -219,7 +242,7 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": workload_config(args.log_n, args.batch),
+        "config": workload_config(args.log_n, args.batch, args.kind),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
                          "kind": "port", "sample": sample_desc},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -430,25 +453,29 @@ def run_ours(args) -> None:
 
     B_ = args.batch
     L = args.log_n
+    kind = args.kind
     dev = capi.DeviceHandle(local)
     n = 1 << L
+    per_item = elems_per_item(L, kind)
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    x = torch.complex(torch.rand(B_, n, device="cuda", generator=g) * 2 - 1,
-                      torch.rand(B_, n, device="cuda", generator=g) * 2 - 1)
+    x = torch.complex(torch.rand(B_, per_item, device="cuda", generator=g) * 2 - 1,
+                      torch.rand(B_, per_item, device="cuda", generator=g) * 2 - 1)
     y = torch.empty_like(x)
     z = torch.empty_like(x)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
-    launches_per_step = 2 * capi.launch_count(L, B_, 1)
+    launches_per_step = 2 * capi.launch_count(L, B_, 1 if kind == "1d" else 2)
+    fft = capi.fft_1d if kind == "1d" else capi.fft_2d
+    fft_host = capi.fft_1d_host if kind == "1d" else capi.fft_2d_host
 
     def step(events=None):
         if events is not None:
             events[0].record(stream)
-        capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), L, B_, "forward", False, sp)
+        fft(dev, x.data_ptr(), y.data_ptr(), L, B_, "forward", False, sp)
         if events is not None:
             events[1].record(stream)
             events[2].record(stream)
-        capi.fft_1d(dev, y.data_ptr(), z.data_ptr(), L, B_, "inverse", True, sp)
+        fft(dev, y.data_ptr(), z.data_ptr(), L, B_, "inverse", True, sp)
         if events is not None:
             events[3].record(stream)
 
@@ -483,11 +510,13 @@ def run_ours(args) -> None:
                 [ev[2].elapsed_time(ev[3]) for ev in per_launch]
     avg_launch_ms = max_over_ranks(sum(launch_ms) / len(launch_ms))
 
-    bytes_per_pass = BYTES_PER_ELEM_PASS * n * B_
+    # Algorithmic bytes of one transform (forward or inverse): 16 B per element
+    # per counted pass.
+    bytes_per_pass = BYTES_PER_ELEM_PASS * per_item * B_ * passes_counted(kind)
     value = world * args.steps * 2 * bytes_per_pass / (elapsed_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = bytes_per_pass / (avg_launch_ms * 1e-3) / 1e9
-    traffic = profiled_traffic(L, B_)
+    traffic = profiled_traffic(L, B_) if kind == "1d" else None
 
     # End to end through the public host-pointer API with pinned buffers.
     e2e = None
@@ -495,12 +524,12 @@ def run_ours(args) -> None:
         hx = x.cpu().pin_memory()
         hy = torch.empty_like(hx).pin_memory()
         hz = torch.empty_like(hx).pin_memory()
-        capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), L, B_, "forward", False)
+        fft_host(dev, hx.data_ptr(), hy.data_ptr(), L, B_, "forward", False)
         barrier()
         t0 = time.perf_counter()
         for _ in range(args.e2e_steps):
-            capi.fft_1d_host(dev, hx.data_ptr(), hy.data_ptr(), L, B_, "forward", False)
-            capi.fft_1d_host(dev, hy.data_ptr(), hz.data_ptr(), L, B_, "inverse", True)
+            fft_host(dev, hx.data_ptr(), hy.data_ptr(), L, B_, "forward", False)
+            fft_host(dev, hy.data_ptr(), hz.data_ptr(), L, B_, "inverse", True)
         t_e2e = max_over_ranks(time.perf_counter() - t0)
         barrier()
         e2e_err = float((hz - hx).abs().max() / hx.abs().max())
@@ -508,23 +537,24 @@ def run_ours(args) -> None:
             raise SystemExit(f"e2e round-trip error {e2e_err} exceeds 1e-4")
         e2e = {"value": round(world * args.e2e_steps * 2 * bytes_per_pass / t_e2e / 1e9, 3),
                "unit": UNIT,
-               "h2d_bytes_per_step": 2 * 8 * n * B_,
-               "d2h_bytes_per_step": 2 * 8 * n * B_,
+               "h2d_bytes_per_step": 2 * 8 * per_item * B_,
+               "d2h_bytes_per_step": 2 * 8 * per_item * B_,
                "steps": args.e2e_steps,
-               "path": "ferrum_fft_1d_c2c_pow2_host (C ABI), pinned host buffers, forward + inverse"}
+               "path": f"ferrum_fft_{kind}_c2c_pow2_host (C ABI), pinned host buffers, "
+                       f"forward + inverse"}
 
     extras = None
-    if not args.no_extras and (L, B_) == (LOG_N, BATCH):
+    if not args.no_extras and (kind, L, B_) == ("1d", LOG_N, BATCH):
         extras = measure_extras(capi, dev, x.view(-1), y.view(-1), world, rank, barrier,
                                 max_over_ranks)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_leg(args.cpu_seconds, L, B_)
+        cpu = cpu_baseline_leg(args.cpu_seconds, L, B_, kind)
 
     if rank == 0:
         line = {
-            "metric": METRIC,
+            "metric": METRIC if kind == "1d" else METRIC_2D,
             "value": round(value, 3),
             "unit": UNIT,
             "n_gpus": world,
@@ -536,14 +566,16 @@ def run_ours(args) -> None:
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic",
-            "config": workload_config(L, B_),
+            "config": workload_config(L, B_, kind),
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
             "transforms_per_s": round(world * args.steps * 2 * B_ / (elapsed_ms * 1e-3), 1),
-            "nominal_gflops": round(world * args.steps * 2 * 5 * n * L * B_ / (elapsed_ms * 1e-3)
-                                    / 1e9, 1),
+            "nominal_gflops": round(world * args.steps * 2 * 5 * per_item * L * passes_counted(kind)
+                                    * B_ / (elapsed_ms * 1e-3) / 1e9, 1),
             "roofline": {
                 "bound": "hbm",
-                "kernel": rows_kernel_name(L),
+                "kernel": rows_kernel_name(L) if kind == "1d" else
+                f"whole 2D {n}x{n} transform ({capi.launch_count(L, B_, 2)} kernels), timed per "
+                f"transform",
                 "achieved": round(achieved, 2),
                 "peak": peak,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
