@@ -80,8 +80,20 @@ struct RowsCfg {
   static constexpr int GROUPS_PER_HALFWARP = (G::T >= 16) ? 1 : (16 / G::T);
   static constexpr int RS = RegionStride<LOGN, LOGP, GROUPS_PER_HALFWARP>::value;
   static constexpr bool NEEDS_SMEM = G::STAGES > 1;
-  static constexpr size_t SMEM_BYTES = NEEDS_SMEM ? (size_t)FPB * RS * sizeof(float2) : 0;
+  // With one or two threads per transform (N <= 32) the CTA's FPB contiguous
+  // transforms are loaded and stored through shared memory: lane-contiguous
+  // global accesses (256 bytes per warp instruction) instead of lanes N
+  // values apart, which cost a cache line per lane and made these sizes
+  // L1-bound. The tile is padded by one slot per 16 values, so each thread's
+  // own values (stride N) also read without bank conflicts.
+  static constexpr bool STAGED = G::T <= 2;
+  static constexpr int TILE = FPB * G::N;
+  static constexpr size_t XCHG_BYTES = NEEDS_SMEM ? (size_t)FPB * RS * sizeof(float2) : 0;
+  static constexpr size_t STAGE_BYTES = STAGED ? (size_t)(TILE + TILE / 16) * sizeof(float2) : 0;
+  static constexpr size_t SMEM_BYTES = XCHG_BYTES > STAGE_BYTES ? XCHG_BYTES : STAGE_BYTES;
 };
+
+__device__ __forceinline__ int tile_pad(int i) { return i + (i >> 4); }
 
 template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT>
 __global__ void __launch_bounds__(RowsCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::THREADS,
@@ -95,8 +107,33 @@ fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, in
   const int t = threadIdx.x % G::T;
   const int64_t f = (int64_t)blockIdx.x * FPB + g;
   const bool valid = f < nfft;
+  float2* sm = smem + (C::NEEDS_SMEM ? g * C::RS : 0);
 
   float2 v[G::P];
+  if constexpr (C::STAGED) {
+    if (log_block >= LOGN) {  // unblocked store (the blocked one keeps the direct path)
+      const int64_t base = (int64_t)blockIdx.x * C::TILE;
+      const int64_t total = nfft * G::N;
+#pragma unroll
+      for (int i = threadIdx.x; i < C::TILE; i += C::THREADS)
+        smem[tile_pad(i)] = base + i < total ? conj_if(ld_stream(in + base + i), CONJ_IN)
+                                             : make_float2(0.f, 0.f);
+      __syncthreads();
+#pragma unroll
+      for (int m = 0; m < G::P; ++m) v[m] = smem[tile_pad(g * G::N + t + G::T * m)];
+      __syncthreads();  // the exchange regions overlay the tile
+      run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
+      __syncthreads();
+#pragma unroll
+      for (int m = 0; m < G::P; ++m)
+        smem[tile_pad(g * G::N + t + G::T * m)] = epilogue<CONJ_OUT>(v[m], scale);
+      __syncthreads();
+#pragma unroll
+      for (int i = threadIdx.x; i < C::TILE; i += C::THREADS)
+        if (base + i < total) st_stream(out + base + i, smem[tile_pad(i)]);
+      return;
+    }
+  }
   if (valid) {
     const float2* src = in + f * G::N + t;
 #pragma unroll
@@ -105,7 +142,6 @@ fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, in
 #pragma unroll
     for (int m = 0; m < G::P; ++m) v[m] = make_float2(0.f, 0.f);
   }
-  float2* sm = smem + (C::NEEDS_SMEM ? g * C::RS : 0);
   if constexpr (G::T <= 32)
     run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
   else
