@@ -66,14 +66,17 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the secondary measurements (other configs, 2D 16384^2)")
-    ap.add_argument("--log-n", type=int, default=LOG_N, choices=range(2, 15),
-                    help="log2 of the transform length (default 12: the headline N=4096)")
+    ap.add_argument("--log-n", type=int, default=LOG_N, choices=range(2, 27),
+                    help="log2 of the transform length (default 12: the headline N=4096; "
+                         "15..26 run the multi-pass 1D path, 2D allows up to 14)")
     ap.add_argument("--kind", choices=["1d", "2d"], default="1d",
                     help="2d: the step is a forward + inverse 2D transform of --batch N x N "
                          "images (the 2D config); GB/s count 2 passes per transform")
     ap.add_argument("--batch", type=int, default=None,
                     help="transforms per GPU (default 2 GiB / N; smaller only for profiling)")
     args = ap.parse_args()
+    if args.kind == "2d" and args.log_n > 14:
+        ap.error("--kind 2d needs --log-n <= 14")
     if args.batch is None:
         args.batch = TOTAL_ELEMS >> (args.log_n * (2 if args.kind == "2d" else 1))
     return args
@@ -83,9 +86,10 @@ def elems_per_item(log_n: int, kind: str) -> int:
     return 1 << (log_n * (2 if kind == "2d" else 1))
 
 
-def passes_counted(kind: str) -> int:
-    """Passes the metric counts per transform: 1 (single-pass 1D) or 2 (2D)."""
-    return 2 if kind == "2d" else 1
+def passes_counted(kind: str, log_n: int = 0) -> int:
+    """Passes the metric counts per transform: 1 for single-pass 1D (N <= 2^14),
+    2 for the multi-pass 1D lengths and for 2D, whatever the plan runs."""
+    return 2 if (kind == "2d" or log_n > 14) else 1
 
 
 def workload_config(log_n: int, batch: int, kind: str = "1d") -> dict:
@@ -101,8 +105,8 @@ def workload_config(log_n: int, batch: int, kind: str = "1d") -> dict:
         "inputs": "re/im i.i.d. uniform[-1,1), seeded",
         "l2": (f"no flush: every buffer is {mib:g} MiB > 126 MB L2" if mib > 126 else
                f"L2-resident: buffers of {mib:g} MiB fit the 126 MB L2"),
-        "bytes_counted": f"16 B per complex element per pass, {passes_counted(kind)} pass(es) "
-                         f"per transform",
+        "bytes_counted": f"16 B per complex element per pass, {passes_counted(kind, log_n)} "
+                         f"pass(es) per transform",
     }
 
 
@@ -171,7 +175,7 @@ def time_oracle(transforms: int, threads: int, log_n: int, seed: int = 0, kind: 
         y = oracle.fft_2d(x, log_n, "forward", False, threads=threads)
         oracle.fft_2d(y, log_n, "inverse", True, threads=threads)
     dt = time.perf_counter() - t0
-    return dt, 2 * BYTES_PER_ELEM_PASS * passes_counted(kind) * e
+    return dt, 2 * BYTES_PER_ELEM_PASS * passes_counted(kind, log_n) * e
 
 
 def calibrate_oracle(threads: int, log_n: int, kind: str = "1d") -> float:
@@ -512,7 +516,7 @@ def run_ours(args) -> None:
 
     # Algorithmic bytes of one transform (forward or inverse): 16 B per element
     # per counted pass.
-    bytes_per_pass = BYTES_PER_ELEM_PASS * per_item * B_ * passes_counted(kind)
+    bytes_per_pass = BYTES_PER_ELEM_PASS * per_item * B_ * passes_counted(kind, L)
     value = world * args.steps * 2 * bytes_per_pass / (elapsed_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = bytes_per_pass / (avg_launch_ms * 1e-3) / 1e9
@@ -569,13 +573,14 @@ def run_ours(args) -> None:
             "config": workload_config(L, B_, kind),
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
             "transforms_per_s": round(world * args.steps * 2 * B_ / (elapsed_ms * 1e-3), 1),
-            "nominal_gflops": round(world * args.steps * 2 * 5 * per_item * L * passes_counted(kind)
-                                    * B_ / (elapsed_ms * 1e-3) / 1e9, 1),
+            "nominal_gflops": round(world * args.steps * 2 * 5 * per_item * L
+                                    * (2 if kind == "2d" else 1) * B_ / (elapsed_ms * 1e-3) / 1e9,
+                                    1),
             "roofline": {
                 "bound": "hbm",
-                "kernel": rows_kernel_name(L) if kind == "1d" else
-                f"whole 2D {n}x{n} transform ({capi.launch_count(L, B_, 2)} kernels), timed per "
-                f"transform",
+                "kernel": rows_kernel_name(L) if (kind == "1d" and L <= 14) else
+                f"whole {kind.upper()} N=2^{L} transform ({launches_per_step // 2} kernels), "
+                f"timed per transform",
                 "achieved": round(achieved, 2),
                 "peak": peak,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==

@@ -80,13 +80,13 @@ struct RowsCfg {
   static constexpr int GROUPS_PER_HALFWARP = (G::T >= 16) ? 1 : (16 / G::T);
   static constexpr int RS = RegionStride<LOGN, LOGP, GROUPS_PER_HALFWARP>::value;
   static constexpr bool NEEDS_SMEM = G::STAGES > 1;
-  // With one or two threads per transform (N <= 32) the CTA's FPB contiguous
+  // With at most four threads per transform (N <= 64) the CTA's FPB contiguous
   // transforms are loaded and stored through shared memory: lane-contiguous
   // global accesses (256 bytes per warp instruction) instead of lanes N
   // values apart, which cost a cache line per lane and made these sizes
   // L1-bound. The tile is padded by one slot per 16 values, so each thread's
   // own values (stride N) also read without bank conflicts.
-  static constexpr bool STAGED = G::T <= 2;
+  static constexpr bool STAGED = G::T <= 4;
   static constexpr int TILE = FPB * G::N;
   static constexpr size_t XCHG_BYTES = NEEDS_SMEM ? (size_t)FPB * RS * sizeof(float2) : 0;
   static constexpr size_t STAGE_BYTES = STAGED ? (size_t)(TILE + TILE / 16) * sizeof(float2) : 0;
