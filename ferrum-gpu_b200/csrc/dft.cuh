@@ -110,6 +110,36 @@ constexpr float kSin16 = 0.19509032201612826785f;
 constexpr float kCos3_16 = 0.83146961230254523708f;
 constexpr float kSin3_16 = 0.55557023301960222474f;
 
+// a * W32^j (W32 = exp(-2 pi i / 32)). Meant for exponents that are
+// compile-time constants after unrolling: quarter turns are swaps and sign
+// changes, other angles multiply by constants of the first octant moved by
+// symmetry (cos / sin of 2 pi r / 32 for r <= 4 are 1, kCos16, kCos8,
+// kCos3_16, kCos4 and 0, kSin16, kSin8, kSin3_16, kCos4).
+FERRUM_HD __forceinline__ float2 c_mul_w32(float2 a, int j) {
+  j &= 31;
+  if (j == 0) return a;
+  if (j == 8) return make_float2(a.y, -a.x);
+  if (j == 16) return make_float2(-a.x, -a.y);
+  if (j == 24) return make_float2(-a.y, a.x);
+  const int q = j >> 3, r = j & 7;
+  const float c0[5] = {1.0f, kCos16, kCos8, kCos3_16, kCos4};
+  const float s0[5] = {0.0f, kSin16, kSin8, kSin3_16, kCos4};
+  // (c, s) = (cos, sin) of 2 pi r / 32, r in 1..7
+  const float c = r <= 4 ? c0[r] : s0[8 - r];
+  const float sn = r <= 4 ? s0[r] : c0[8 - r];
+  // exp(-i 2 pi j / 32) = (-i)^q (c - i s)
+  float2 w;
+  if (q == 0)
+    w = make_float2(c, -sn);
+  else if (q == 1)
+    w = make_float2(-sn, -c);
+  else if (q == 2)
+    w = make_float2(-c, sn);
+  else
+    w = make_float2(sn, c);
+  return c_mul(a, w);
+}
+
 // Radix 32 = radix-2 split over two radix-16 DFTs:
 // X[k] = E[k] + W32^k O[k], X[k+16] = E[k] - W32^k O[k].
 FERRUM_HD __forceinline__ void dft32(float2 (&u)[32]) {

@@ -167,13 +167,15 @@ fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, in
 // ----------------------------------------------------------------------------
 // Strided pass. `nfft` length-N transforms, transform f = (o, j, c) with c the
 // fastest index (c < 2^log_w, j < 2^log_j): element e is read at
-//   in [o*in_o  + j*in_j  + c + e*in_e]
+//   in [o*in_o  + j*in_j  + c*in_c  + e*in_e]
 // and output k is written to
-//   out[o*out_o + j*out_j + c + k*out_e],
+//   out[o*out_o + j*out_j + c*out_c + k*out_e],
 // multiplied, when log_m > 0, by the twiddle W_M^((c*j*tcj + (c*tc + j*tj)*k) mod M),
-// M = 2^log_m. Adjacent columns c are adjacent in memory on both sides, so a
-// CTA of FPB columns reads and writes FPB*8-byte row segments; lanes run over
-// the columns first. Used for 2D column passes (one or two sub-passes), the
+// M = 2^log_m. Usually adjacent columns c are adjacent in memory on both
+// sides (in_c = out_c = 1, what every plan uses), so a CTA of FPB columns
+// reads and writes FPB*8-byte row segments; lanes run over the columns first.
+// (Contiguous rows stored transposed, in_c = N, in_e = 1, measured slower than
+// fft_rows_t_kernel for the two-pass 1D rows: 32-byte input segments.) Used for 2D column passes (one or two sub-passes), the
 // column passes of the multi-pass 1D transform and the distributed column
 // pass.
 struct PassArgs {
@@ -182,6 +184,7 @@ struct PassArgs {
   int log_j;
   int64_t in_o, in_j, in_e;
   int64_t out_o, out_j, out_e;
+  int64_t in_c, out_c;  // column strides (1 for adjacent columns)
   uint32_t tcj, tc, tj;
   int log_m;
   const float2* tw_lo;
@@ -288,8 +291,8 @@ fft_pass_kernel(const float2* in, float2* out, const float2* __restrict__ tw, Pa
   const uint32_t ts = TW ? pass_tw_step((uint32_t)c, (uint32_t)j, a.tc, a.tj) : 0u;
   const uint32_t mask = TW ? (1u << a.log_m) - 1u : 0u;
   float2* sm = smem + (C::SMEM_BYTES ? cl * C::RS : 0);
-  const float2* src = in + o * a.in_o + j * a.in_j + c;
-  float2* dst = out + o * a.out_o + j * a.out_j + c;
+  const float2* src = in + o * a.in_o + j * a.in_j + c * a.in_c;
+  float2* dst = out + o * a.out_o + j * a.out_j + c * a.out_c;
   if constexpr (FPB == 1 && G::T <= 32)
     strided_unit<LOGN, LOGP, CONJ_IN, CONJ_OUT, TW, true, true>(
         src, a.in_e, dst, a.out_e, valid, t, sm, tw, tb + ts * (uint32_t)t, ts * (uint32_t)G::T,

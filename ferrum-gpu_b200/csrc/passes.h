@@ -117,9 +117,12 @@ inline PassArgs pass_args(int64_t nfft, int log_w, int log_j, int64_t in_o, int6
   a.out_o = out_o;
   a.out_j = out_j;
   a.out_e = out_e;
+  a.in_c = 1;
+  a.out_c = 1;
   a.scale = 1.0f;
   return a;
 }
+
 
 // The fused column kernel (fft_cols_l2_kernel) per column length: columns per
 // tile W (0 = the length keeps two separate sub-passes), threads and resident

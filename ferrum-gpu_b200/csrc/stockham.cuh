@@ -91,13 +91,54 @@ FERRUM_HD __forceinline__ void stage_compute(float2 (&v)[1 << LOGP], int t, cons
 #pragma unroll
       for (int r = 17; r < 32; ++r) v[r] = c_mul(v[r], c_mul(w16, w[r - 16]));
     }
-  } else if constexpr (S > 0) {
+  } else if constexpr (S > 0 && (G::P == 32 && R < 16)) {
+    // 32 values per thread and a last radix of 8 or less: most of the
+    // rotations below would be general angles (measured slower at N = 8192),
+    // so every butterfly loads its own twiddles.
     const float2* tws = tw + plan_stage_tw_offset(LOGN, LOGP, S);
 #pragma unroll
     for (int i = 0; i < B; ++i) {
       const int k = (t + G::T * i) & (NS - 1);
 #pragma unroll
       for (int r = 1; r < R; ++r) v[i + r * B] = c_mul(v[i + r * B], tw_load(tws + (r - 1) * NS + k));
+    }
+  } else if constexpr (S > 0) {
+    // Last stage with a smaller radix (R < P, B = P/R butterflies per thread;
+    // NS*R = N and T <= NS): butterfly i has k = t + T*i, so
+    //   W_N^(r k) = W_N^(r t) * W_N^(r T i) = W_N^(r t) * W_P^(r i),
+    // R - 1 table loads for all B butterflies and constant rotations (quarter
+    // turns by swaps) instead of (R - 1) * B lane-scattered loads, which made
+    // the strided passes L1-bound (N = 1024: 0.65 -> 0.63 ms, N = 16384:
+    // 0.85 -> 0.79 ms per 2 GiB).
+    static_assert(G::T <= NS, "last stage: T <= NS");
+    const float2* tws = tw + plan_stage_tw_offset(LOGN, LOGP, S);
+    const int k = t & (NS - 1);
+    if constexpr (R == 16) {
+      float2 w[16];
+      w[1] = tw_load(tws + 0 * NS + k);
+      w[2] = tw_load(tws + 1 * NS + k);
+      w[4] = tw_load(tws + 3 * NS + k);
+      w[8] = tw_load(tws + 7 * NS + k);
+      w[3] = c_mul(w[1], w[2]);
+      w[5] = c_mul(w[1], w[4]);
+      w[6] = c_mul(w[2], w[4]);
+      w[7] = c_mul(w[3], w[4]);
+#pragma unroll
+      for (int r = 9; r < 16; ++r) w[r] = c_mul(w[r - 8], w[8]);
+#pragma unroll
+      for (int i = 0; i < B; ++i)
+#pragma unroll
+        for (int r = 1; r < R; ++r)
+          v[i + r * B] = c_mul(c_mul_w32(v[i + r * B], (r * i) * (32 / G::P)), w[r]);
+    } else {
+      // One twiddle live at a time: it serves input r of all B butterflies.
+#pragma unroll
+      for (int r = 1; r < R; ++r) {
+        const float2 w = tw_load(tws + (r - 1) * NS + k);
+#pragma unroll
+        for (int i = 0; i < B; ++i)
+          v[i + r * B] = c_mul(c_mul_w32(v[i + r * B], (r * i) * (32 / G::P)), w);
+      }
     }
   }
 #pragma unroll

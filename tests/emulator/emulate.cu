@@ -210,7 +210,8 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst, float2* ws) {
       for (int64_t f = 0; f < a.nfft; ++f) {
         int64_t o, j, c;
         pass_index(f, a.log_w, a.log_j, o, j, c);
-        const int64_t ib = o * a.in_o + j * a.in_j + c, ob = o * a.out_o + j * a.out_j + c;
+        const int64_t ib = o * a.in_o + j * a.in_j + c * a.in_c,
+                      ob = o * a.out_o + j * a.out_j + c * a.out_c;
         for (int64_t e = 0; e < n; ++e) x[e] = conj_if(src[ib + e * a.in_e], d.conj_in);
         if (int rc = run_group(d.log_n, x.data(), x.data(), stw)) return rc;
         if (a.log_m > 0) {
