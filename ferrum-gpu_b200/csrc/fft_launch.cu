@@ -17,11 +17,12 @@ constexpr int kRowsThreads = 256;   // batched rows: 256 threads per CTA up to N
 // element and costs one resident CTA per SM, and the kernel is bound by the
 // L1/shared pipe and issue rate rather than by DRAM latency. It stays off.
 constexpr bool kRowsTmaEnabled = false;
-// Sizes that use fft_rows_pf_kernel (prefetch into the exchange buffer):
-// measured faster only at N = 16384 (0.99 vs 1.11 ms per 2 GiB), where one CTA
-// fills an SM and its load phase was exposed; at N = 8192 (two CTAs per SM)
-// and below it was slower.
-constexpr bool rows_pf_enabled(int log_n) { return log_n == 14; }
+// Sizes that use fft_rows_pf_kernel (prefetch into the exchange buffer): the
+// sizes with 32 values per thread, where one or two CTAs fill an SM and the
+// load phase is otherwise exposed (per 2 GiB: N = 16384 0.99 -> 0.85 ms,
+// N = 8192 0.79 -> 0.73 ms); with 16 values per thread (N <= 4096, four or
+// more CTAs per SM) it measured slower.
+constexpr bool rows_pf_enabled(int log_n) { return log_n == 13 || log_n == 14; }
 constexpr int kColsThreads = 512;   // strided passes: up to 16 columns / rows per CTA
 
 constexpr int rows_fpb(int log_n) {
