@@ -23,8 +23,7 @@
 //
 // The host-side name of a __device__ array is not a device address, so the
 // first call on each device looks the address up with cudaGetSymbolAddress
-// while that device is current, and caches it. That first call per device
-// should therefore come before any stream capture.
+// while that device is current, and caches it.
 #include <cuda_runtime.h>
 
 #include <mutex>

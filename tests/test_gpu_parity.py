@@ -185,13 +185,17 @@ def test_2d(capi, dev, oracle_mod, log_n, direction, normalize):
     assert max_rel_err(got, ref) < TOL
 
 
-def test_2d_8192_in_place(capi, dev, oracle_mod):
-    log_n = 13
-    rng = np.random.default_rng(5113)
+@pytest.mark.parametrize("log_n,batch", [(11, 2), (12, 3), (13, 1)])
+@pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
+def test_2d_in_place(capi, dev, oracle_mod, log_n, batch, direction, normalize):
+    # N = 2048: one column pass; N = 4096: the fused two-sub-pass column
+    # kernel (three images: tiles of more than one image per CTA); N = 8192:
+    # separate sub-passes; every plan then runs the rows in place.
+    rng = np.random.default_rng(5100 + log_n)
     n = 1 << log_n
-    x = rand_c64(rng, (n, n), "normal")
-    got = run_2d(capi, dev, x, log_n, "forward", False, inplace=True)
-    ref = oracle_mod.fft_2d(x, log_n, "forward", False, threads=8)
+    x = rand_c64(rng, (batch, n, n), "normal")
+    got = run_2d(capi, dev, x, log_n, direction, normalize, inplace=True)
+    ref = oracle_mod.fft_2d(x, log_n, direction, normalize, threads=8)
     assert max_rel_err(got, ref) < TOL
 
 
