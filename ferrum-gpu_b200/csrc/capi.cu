@@ -7,6 +7,8 @@
 // re-uploaded its twiddles, allocated input/output/twiddle buffers and
 // conjugated on the host on every call (lib.rs:105-140, :237-247).
 #include <cuda_runtime.h>
+
+#include <initializer_list>
 #include <math.h>
 #include <string.h>
 
@@ -373,6 +375,91 @@ ferrum_status ferrum_fft_1d_c2c_pow2(ferrum_device* dev, const void* in_dev, voi
   e = cudaFreeAsync(ws, (cudaStream_t)stream);
   if (s == FERRUM_OK && e != cudaSuccess) return cuda_error(e, "cudaFreeAsync(workspace)");
   return s;
+}
+
+ferrum_status ferrum_fft_1d_c2c_pow2_split(ferrum_device* dev, const float* in_re,
+                                           const float* in_im, float* out_re, float* out_im,
+                                           int log_n, size_t batch, int direction, int normalize,
+                                           void* stream) {
+  clear_error();
+  if (ferrum_status s = check_device(dev)) return s;
+  if (ferrum_status s =
+          check_common(log_n, 2, kMaxSinglePassLogN, batch, direction, "fft_1d_c2c_pow2_split"))
+    return s;
+  if (!in_re || !in_im || !out_re || !out_im)
+    return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2_split: NULL array");
+  if ((out_re == in_im && out_re != in_re) || (out_im == in_re && out_im != in_im))
+    return set_error(FERRUM_ERR_INVALID_ARG,
+                     "fft_1d_c2c_pow2_split: out_re / out_im may only alias in_re / in_im");
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  const bool inv = direction < 0;
+  const float scale = (inv && normalize) ? 1.0f / (float)((int64_t)1 << log_n) : 1.0f;
+  cudaError_t e = launch_rows_split(log_n, inv, inv, in_re, in_im, out_re, out_im,
+                                    stage_table(dev, log_n), (int64_t)batch, scale,
+                                    (cudaStream_t)stream);
+  return e == cudaSuccess ? FERRUM_OK : cuda_error(e, "split-layout row pass launch");
+}
+
+namespace {
+ferrum_status check_elementwise(ferrum_device* dev, size_t n, std::initializer_list<const void*> ptrs,
+                                const char* what) {
+  if (ferrum_status s = check_device(dev)) return s;
+  if (n == 0) return set_error(FERRUM_ERR_INVALID_ARG, std::string(what) + ": n must be positive");
+  for (const void* p : ptrs)
+    if (p == nullptr) return set_error(FERRUM_ERR_INVALID_ARG, std::string(what) + ": NULL array");
+  return FERRUM_OK;
+}
+}  // namespace
+
+ferrum_status ferrum_cmul_interleaved(ferrum_device* dev, const void* a, const void* b, void* out,
+                                      size_t n, void* stream) {
+  clear_error();
+  if (ferrum_status s = check_elementwise(dev, n, {a, b, out}, "cmul_interleaved")) return s;
+  if (!is_aligned8(a) || !is_aligned8(b) || !is_aligned8(out))
+    return set_error(FERRUM_ERR_INVALID_ARG, "cmul_interleaved: arrays must be 8-byte aligned");
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  cudaError_t e = launch_cmul_interleaved((const float2*)a, (const float2*)b, (float2*)out,
+                                          (int64_t)n, (cudaStream_t)stream);
+  return e == cudaSuccess ? FERRUM_OK : cuda_error(e, "cmul_interleaved launch");
+}
+
+ferrum_status ferrum_cmul_split(ferrum_device* dev, const float* a_re, const float* a_im,
+                                const float* b_re, const float* b_im, float* out_re,
+                                float* out_im, size_t n, void* stream) {
+  clear_error();
+  if (ferrum_status s =
+          check_elementwise(dev, n, {a_re, a_im, b_re, b_im, out_re, out_im}, "cmul_split"))
+    return s;
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  cudaError_t e = launch_cmul_split(a_re, a_im, b_re, b_im, out_re, out_im, (int64_t)n,
+                                    (cudaStream_t)stream);
+  return e == cudaSuccess ? FERRUM_OK : cuda_error(e, "cmul_split launch");
+}
+
+ferrum_status ferrum_deinterleave(ferrum_device* dev, const void* in, float* out_re, float* out_im,
+                                  size_t n, void* stream) {
+  clear_error();
+  if (ferrum_status s = check_elementwise(dev, n, {in, out_re, out_im}, "deinterleave")) return s;
+  if (!is_aligned8(in)) return set_error(FERRUM_ERR_INVALID_ARG, "deinterleave: input must be 8-byte aligned");
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  cudaError_t e = launch_deinterleave((const float2*)in, out_re, out_im, (int64_t)n,
+                                      (cudaStream_t)stream);
+  return e == cudaSuccess ? FERRUM_OK : cuda_error(e, "deinterleave launch");
+}
+
+ferrum_status ferrum_interleave(ferrum_device* dev, const float* re, const float* im, void* out,
+                                size_t n, void* stream) {
+  clear_error();
+  if (ferrum_status s = check_elementwise(dev, n, {re, im, out}, "interleave")) return s;
+  if (!is_aligned8(out)) return set_error(FERRUM_ERR_INVALID_ARG, "interleave: output must be 8-byte aligned");
+  DeviceGuard guard(dev->ordinal);
+  if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  cudaError_t e = launch_interleave(re, im, (float2*)out, (int64_t)n, (cudaStream_t)stream);
+  return e == cudaSuccess ? FERRUM_OK : cuda_error(e, "interleave launch");
 }
 
 ferrum_status ferrum_fft_2d_c2c_pow2(ferrum_device* dev, const void* in_dev, void* out_dev,

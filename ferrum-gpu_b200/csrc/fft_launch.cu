@@ -5,6 +5,7 @@
 #include "fft_kernels.cuh"
 #include "fft_launch.h"
 #include "fft_rows_tma.cuh"
+#include "layout_kernels.cuh"
 #include "passes.h"
 
 namespace ferrum {
@@ -271,6 +272,27 @@ cudaError_t rows_gather_impl(const PeerPtrs& src, float2* out, const float2* tw,
   return cudaGetLastError();
 }
 
+template <int LOGN, bool CI, bool CO>
+cudaError_t rows_split_impl(const float* in_re, const float* in_im, float* out_re, float* out_im,
+                            const float2* tw, int64_t nfft, float scale, cudaStream_t s) {
+  constexpr int LOGP = plan_log_p(LOGN);
+  constexpr int FPB = rows_fpb(LOGN);
+  using C = RowsCfg<LOGN, LOGP, FPB, CI, CO>;
+  auto k = fft_rows_split_kernel<LOGN, LOGP, FPB, CI, CO>;
+  static std::atomic<uint64_t> smem_done{0};
+  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
+  if (e != cudaSuccess) return e;
+  k<<<(unsigned)ceil_div(nfft, FPB), C::THREADS, C::SMEM_BYTES, s>>>(in_re, in_im, out_re, out_im,
+                                                                     tw, nfft, scale);
+  return cudaGetLastError();
+}
+
+unsigned elementwise_grid(int64_t n) {
+  int64_t g = (n + 255) / 256;
+  if (g > 148 * 16) g = 148 * 16;
+  return (unsigned)(g < 1 ? 1 : g);
+}
+
 // out[r * out_ld + p*bw + c] = in[p*in_bs + r*bw + c] for p < nblocks, r < rows,
 // c < bw; one thread moves two complex values.
 __global__ void __launch_bounds__(256) block_gather_kernel(const float4* __restrict__ in,
@@ -362,6 +384,35 @@ cudaError_t launch_dist_barrier(const PeerFlags& flags, int rank, int nranks, ui
   return cudaGetLastError();
 }
 
+cudaError_t launch_cmul_interleaved(const float2* a, const float2* b, float2* out, int64_t n,
+                                    cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  cmul_interleaved_kernel<<<elementwise_grid(n), 256, 0, stream>>>(a, b, out, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cmul_split(const float* a_re, const float* a_im, const float* b_re,
+                              const float* b_im, float* o_re, float* o_im, int64_t n,
+                              cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  cmul_split_kernel<<<elementwise_grid(n), 256, 0, stream>>>(a_re, a_im, b_re, b_im, o_re, o_im, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_deinterleave(const float2* in, float* re, float* im, int64_t n,
+                                cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  deinterleave_kernel<<<elementwise_grid(n), 256, 0, stream>>>(in, re, im, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_interleave(const float* re, const float* im, float2* out, int64_t n,
+                              cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  interleave_kernel<<<elementwise_grid(n), 256, 0, stream>>>(re, im, out, n);
+  return cudaGetLastError();
+}
+
 #define FERRUM_CASE_2_14(X) \
   X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
 
@@ -375,6 +426,26 @@ cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in
   case L:    \
     return rows_dispatch<L>(conj_in, conj_out, in, out, tw, nfft, scale, log_block, block_rows, \
                             err_flag, stream);
+    FERRUM_CASE_2_14(X)
+#undef X
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_rows_split(int log_n, bool conj_in, bool conj_out, const float* in_re,
+                              const float* in_im, float* out_re, float* out_im, const float2* tw,
+                              int64_t nfft, float scale, cudaStream_t stream) {
+  switch (log_n) {
+#define X(L)                                                                                  \
+  case L:                                                                                     \
+    if (conj_in && conj_out)                                                                  \
+      return rows_split_impl<L, true, true>(in_re, in_im, out_re, out_im, tw, nfft, scale, stream); \
+    if (conj_in)                                                                              \
+      return rows_split_impl<L, true, false>(in_re, in_im, out_re, out_im, tw, nfft, scale, stream); \
+    if (conj_out)                                                                             \
+      return rows_split_impl<L, false, true>(in_re, in_im, out_re, out_im, tw, nfft, scale, stream); \
+    return rows_split_impl<L, false, false>(in_re, in_im, out_re, out_im, tw, nfft, scale, stream);
     FERRUM_CASE_2_14(X)
 #undef X
     default:

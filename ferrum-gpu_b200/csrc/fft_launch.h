@@ -67,4 +67,20 @@ cudaError_t launch_peer_block_gather(const PeerPtrs& src, float2* out, int nrank
 cudaError_t launch_dist_barrier(const PeerFlags& flags, int rank, int nranks, uint32_t epoch,
                                 uint64_t timeout_ns, int* err, cudaStream_t stream);
 
+// Split (planar) layout, layout_kernels.cuh: batched single-pass transform
+// (2 <= log_n <= 14) on separate real / imaginary float arrays, and the
+// elementwise helpers over n complex values.
+cudaError_t launch_rows_split(int log_n, bool conj_in, bool conj_out, const float* in_re,
+                              const float* in_im, float* out_re, float* out_im, const float2* tw,
+                              int64_t nfft, float scale, cudaStream_t stream);
+cudaError_t launch_cmul_interleaved(const float2* a, const float2* b, float2* out, int64_t n,
+                                    cudaStream_t stream);
+cudaError_t launch_cmul_split(const float* a_re, const float* a_im, const float* b_re,
+                              const float* b_im, float* o_re, float* o_im, int64_t n,
+                              cudaStream_t stream);
+cudaError_t launch_deinterleave(const float2* in, float* re, float* im, int64_t n,
+                                cudaStream_t stream);
+cudaError_t launch_interleave(const float* re, const float* im, float2* out, int64_t n,
+                              cudaStream_t stream);
+
 }  // namespace ferrum

@@ -46,6 +46,11 @@ SIGNATURES = {
     "ferrum_fft_1d_c2c_pow2_noalloc": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
     "ferrum_fft_2d_c2c_pow2": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
     "ferrum_fft_1d_c2c_pow2_host": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i]),
+    "ferrum_fft_1d_c2c_pow2_split": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _sz, _i, _i, _vp]),
+    "ferrum_cmul_interleaved": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
+    "ferrum_cmul_split": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ferrum_deinterleave": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
+    "ferrum_interleave": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
     "ferrum_fft_2d_c2c_pow2_host": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i]),
     "ferrum_fft_workspace_bytes": (_i, [_i, _sz, _i, ctypes.POINTER(_sz)]),
     "ferrum_fft_launch_count": (_i, [_i, _sz, _i, ctypes.POINTER(_i)]),
@@ -175,6 +180,32 @@ def fft_2d_host(dev: DeviceHandle, in_ptr: int, out_ptr: int, log_n: int, batch:
                 direction="forward", normalize: bool = False) -> None:
     check(lib().ferrum_fft_2d_c2c_pow2_host(dev.ptr, in_ptr, out_ptr, log_n, batch,
                                             _dir(direction), int(bool(normalize))))
+
+
+def fft_1d_split(dev: DeviceHandle, in_re: int, in_im: int, out_re: int, out_im: int,
+                 log_n: int, batch: int, direction="forward", normalize: bool = False,
+                 stream: int = 0) -> None:
+    """Batched 1D transform on split (planar) float arrays (2 <= log_n <= 14)."""
+    check(lib().ferrum_fft_1d_c2c_pow2_split(dev.ptr, in_re, in_im, out_re, out_im, log_n, batch,
+                                             _dir(direction), int(bool(normalize)), stream))
+
+
+def cmul_interleaved(dev: DeviceHandle, a: int, b: int, out: int, n: int, stream: int = 0) -> None:
+    check(lib().ferrum_cmul_interleaved(dev.ptr, a, b, out, n, stream))
+
+
+def cmul_split(dev: DeviceHandle, a_re: int, a_im: int, b_re: int, b_im: int, out_re: int,
+               out_im: int, n: int, stream: int = 0) -> None:
+    check(lib().ferrum_cmul_split(dev.ptr, a_re, a_im, b_re, b_im, out_re, out_im, n, stream))
+
+
+def deinterleave(dev: DeviceHandle, inp: int, out_re: int, out_im: int, n: int,
+                 stream: int = 0) -> None:
+    check(lib().ferrum_deinterleave(dev.ptr, inp, out_re, out_im, n, stream))
+
+
+def interleave(dev: DeviceHandle, re: int, im: int, out: int, n: int, stream: int = 0) -> None:
+    check(lib().ferrum_interleave(dev.ptr, re, im, out, n, stream))
 
 
 def workspace_bytes(log_n: int, batch: int, kind: int = 1) -> int:

@@ -121,6 +121,34 @@ ferrum_status ferrum_fft_2d_c2c_pow2_host(ferrum_device *dev, const void *in_hos
                                           void *out_host, int log_n, size_t batch,
                                           int direction, int normalize);
 
+/* ---------------------------------------------------------------------------
+ * Split (planar) complex layout: real and imaginary parts in two float
+ * arrays. Replaces the reference's split twins and layout helpers
+ * (crates/ferrum-gpu-fft-kernels/src/kernels_body.rs:508-626
+ * fft_c2c_1024_split; 1614-1672 cmul_interleaved, cmul_split, deinterleave,
+ * interleave), which it only launches from its layout benchmarks.
+ */
+/* Batched 1D transform on [batch][N] float arrays, single pass:
+ * 2 <= log_n <= 14. Same results as ferrum_fft_1d_c2c_pow2 on the
+ * interleaved data. out_re / out_im may be in_re / in_im (in place). */
+ferrum_status ferrum_fft_1d_c2c_pow2_split(ferrum_device *dev, const float *in_re,
+                                           const float *in_im, float *out_re, float *out_im,
+                                           int log_n, size_t batch, int direction, int normalize,
+                                           void *stream);
+/* out[i] = a[i] * b[i] for n interleaved complex values (products and sums
+ * rounded separately, as the reference's kernel writes them). */
+ferrum_status ferrum_cmul_interleaved(ferrum_device *dev, const void *a, const void *b, void *out,
+                                      size_t n, void *stream);
+/* The same on split arrays. */
+ferrum_status ferrum_cmul_split(ferrum_device *dev, const float *a_re, const float *a_im,
+                                const float *b_re, const float *b_im, float *out_re,
+                                float *out_im, size_t n, void *stream);
+/* n interleaved complex values to two float arrays, and back. */
+ferrum_status ferrum_deinterleave(ferrum_device *dev, const void *in, float *out_re,
+                                  float *out_im, size_t n, void *stream);
+ferrum_status ferrum_interleave(ferrum_device *dev, const float *re, const float *im, void *out,
+                                size_t n, void *stream);
+
 /* Workspace bytes a call needs: kind 1 = 1D, kind 2 = 2D. */
 ferrum_status ferrum_fft_workspace_bytes(int log_n, size_t batch, int kind, size_t *bytes);
 
