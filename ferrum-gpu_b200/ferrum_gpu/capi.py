@@ -51,6 +51,16 @@ SIGNATURES = {
     "ferrum_cmul_split": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ferrum_deinterleave": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
     "ferrum_interleave": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
+    "ferrum_buffer_alloc_zeros": (_i, [_vp, _sz, ctypes.POINTER(_vp)]),
+    "ferrum_buffer_free": (_i, [_vp, _vp]),
+    "ferrum_copy_h2d": (_i, [_vp, _vp, _vp, _sz]),
+    "ferrum_copy_d2h": (_i, [_vp, _vp, _vp, _sz]),
+    "ferrum_module_load": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "ferrum_module_unload": (_i, [_vp]),
+    "ferrum_module_kernel": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "ferrum_launch": (_i, [_vp, _vp, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint),
+                           ctypes.c_uint, ctypes.POINTER(_vp), _vp]),
+    "ferrum_stream_sync": (_i, [_vp, _vp]),
     "ferrum_fft_2d_c2c_pow2_host": (_i, [_vp, _vp, _vp, _i, _sz, _i, _i]),
     "ferrum_fft_workspace_bytes": (_i, [_i, _sz, _i, ctypes.POINTER(_sz)]),
     "ferrum_fft_launch_count": (_i, [_i, _sz, _i, ctypes.POINTER(_i)]),
@@ -206,6 +216,45 @@ def deinterleave(dev: DeviceHandle, inp: int, out_re: int, out_im: int, n: int,
 
 def interleave(dev: DeviceHandle, re: int, im: int, out: int, n: int, stream: int = 0) -> None:
     check(lib().ferrum_interleave(dev.ptr, re, im, out, n, stream))
+
+
+class Module:
+    """A loaded kernel module (PTX text or a cubin / fatbin image)."""
+
+    def __init__(self, dev: DeviceHandle, image: bytes):
+        if isinstance(image, str):
+            image = image.encode()
+        if not image.endswith(b"\0") and image[:4] != b"\x7fELF":
+            image = image + b"\0"   # PTX text is read up to its NUL
+        self._image = image
+        h = _vp()
+        check(lib().ferrum_module_load(dev.ptr, image, ctypes.byref(h)))
+        self.ptr = h
+        self.dev = dev
+
+    def kernel(self, name: str) -> int:
+        k = _vp()
+        check(lib().ferrum_module_kernel(self.ptr, name.encode(), ctypes.byref(k)))
+        return k.value
+
+    def launch(self, kernel: int, grid, block, args, shared_bytes: int = 0,
+               stream: int = 0) -> None:
+        """`args`: ctypes values (c_void_p, c_int, c_float, ...) in kernel order."""
+        g = (ctypes.c_uint * 3)(*(tuple(grid) + (1,) * (3 - len(grid))))
+        b = (ctypes.c_uint * 3)(*(tuple(block) + (1,) * (3 - len(block))))
+        ptrs = (_vp * len(args))(*(ctypes.cast(ctypes.pointer(a), _vp) for a in args))
+        check(lib().ferrum_launch(self.dev.ptr, kernel, g, b, shared_bytes, ptrs, stream))
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None) and self.ptr.value:
+            lib().ferrum_module_unload(self.ptr)
+            self.ptr = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def workspace_bytes(log_n: int, batch: int, kind: int = 1) -> int:

@@ -149,6 +149,35 @@ ferrum_status ferrum_deinterleave(ferrum_device *dev, const void *in, float *out
 ferrum_status ferrum_interleave(ferrum_device *dev, const float *re, const float *im, void *out,
                                 size_t n, void *stream);
 
+/* ---------------------------------------------------------------------------
+ * Kernel-module substrate: the operations of the reference's backend contract
+ * (crates/ferrum-gpu-core/src/backend.rs:12-77 alloc_zeros, copy_h2d,
+ * copy_d2h, load_module, get_kernel, launch, sync_stream) for callers that
+ * bring their own kernels, as its vector-add examples do.
+ */
+typedef struct ferrum_module ferrum_module;
+/* `bytes` of device memory, zero-filled; release with ferrum_buffer_free. */
+ferrum_status ferrum_buffer_alloc_zeros(ferrum_device *dev, size_t bytes, void **out);
+ferrum_status ferrum_buffer_free(ferrum_device *dev, void *buf);
+/* Synchronous copies between host and device memory. */
+ferrum_status ferrum_copy_h2d(ferrum_device *dev, void *dst_dev, const void *src_host, size_t bytes);
+ferrum_status ferrum_copy_d2h(ferrum_device *dev, void *dst_host, const void *src_dev, size_t bytes);
+/* Loads a module image: NUL-terminated PTX text (compiled for the device
+ * when loaded) or a cubin / fatbin image. */
+ferrum_status ferrum_module_load(ferrum_device *dev, const void *image, ferrum_module **out);
+ferrum_status ferrum_module_unload(ferrum_module *module);
+/* Kernel `name` (its mangled name for C++ kernels) of a loaded module; the
+ * handle stays valid until the module is unloaded. */
+ferrum_status ferrum_module_kernel(ferrum_module *module, const char *name, void **kernel_out);
+/* Launches `kernel` with grid / block dimensions (x, y, z), dynamic shared
+ * bytes and `args` (an array of pointers to each argument value), on
+ * `stream` (NULL: the default stream). Asynchronous. */
+ferrum_status ferrum_launch(ferrum_device *dev, void *kernel, const unsigned grid[3],
+                            const unsigned block[3], unsigned shared_bytes, void **args,
+                            void *stream);
+/* Waits for all work on `stream`. */
+ferrum_status ferrum_stream_sync(ferrum_device *dev, void *stream);
+
 /* Workspace bytes a call needs: kind 1 = 1D, kind 2 = 2D. */
 ferrum_status ferrum_fft_workspace_bytes(int log_n, size_t batch, int kind, size_t *bytes);
 
