@@ -57,6 +57,13 @@ cudaError_t ensure_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done) {
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Every launch below is followed by cudaGetLastError(), which reports the
+// last error of any runtime call in the process. Consuming an earlier,
+// unrelated error (a failed lookup or allocation by the caller) first keeps it
+// from being reported as a failure of this launch; sticky errors persist
+// and are still reported.
+inline void clear_stale_error() { (void)cudaGetLastError(); }
+
 template <int LOGN, bool CI, bool CO>
 cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t nfft, float scale,
                       int log_block, int64_t block_rows, cudaStream_t s) {
@@ -68,6 +75,7 @@ cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t n
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
   const int64_t blocks = ceil_div(nfft, FPB);
+  clear_stale_error();
   k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, log_block,
                                                         block_rows);
   return cudaGetLastError();
@@ -101,6 +109,7 @@ cudaError_t rows_tma_impl(const float2* in, float2* out, const float2* tw, int64
   }
   const int64_t tiles = ceil_div(nfft, FPB);
   const int64_t grid = tiles < resident ? tiles : resident;
+  clear_stale_error();
   k<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, err);
   return cudaGetLastError();
 }
@@ -133,6 +142,7 @@ cudaError_t rows_pf_impl(const float2* in, float2* out, const float2* tw, int64_
   }
   const int64_t tiles = ceil_div(nfft, FPB);
   const int64_t grid = tiles < resident ? tiles : resident;
+  clear_stale_error();
   k<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, err);
   return cudaGetLastError();
 }
@@ -148,6 +158,7 @@ cudaError_t pass_impl(const float2* in, float2* out, const float2* tw, const Pas
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
   const int64_t blocks = ceil_div(a.nfft, FPB);
+  clear_stale_error();
   k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);
   return cudaGetLastError();
 }
@@ -162,6 +173,7 @@ cudaError_t cols_l2_impl(const float2* in, float2* out, float2* ws, const float2
   if (e != cudaSuccess) return e;
   const int64_t grid = a.tiles < slots ? a.tiles : slots;
   if (grid < 1) return cudaSuccess;
+  clear_stale_error();
   k<<<(unsigned)grid, THREADS, C::SMEM_BYTES, s>>>(in, out, ws, tw1, tw2, a);
   return cudaGetLastError();
 }
@@ -190,6 +202,7 @@ cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const R
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
   const int64_t blocks = ceil_div(a.nfft, FPB);
+  clear_stale_error();
   k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);
   return cudaGetLastError();
 }
@@ -253,6 +266,7 @@ cudaError_t rows_scatter_impl(const float2* in, const PeerPtrs& dst, const float
   static std::atomic<uint64_t> smem_done{0};
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
+  clear_stale_error();
   k<<<(unsigned)ceil_div(nfft, FPB), C::THREADS, C::SMEM_BYTES, s>>>(in, dst, tw, nfft, log_b);
   return cudaGetLastError();
 }
@@ -267,6 +281,7 @@ cudaError_t rows_gather_impl(const PeerPtrs& src, float2* out, const float2* tw,
   static std::atomic<uint64_t> smem_done{0};
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
+  clear_stale_error();
   k<<<(unsigned)ceil_div(nfft, FPB), C::THREADS, C::SMEM_BYTES, s>>>(src, out, tw, nfft, scale,
                                                                      log_b);
   return cudaGetLastError();
@@ -282,6 +297,7 @@ cudaError_t rows_split_impl(const float* in_re, const float* in_im, float* out_r
   static std::atomic<uint64_t> smem_done{0};
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
+  clear_stale_error();
   k<<<(unsigned)ceil_div(nfft, FPB), C::THREADS, C::SMEM_BYTES, s>>>(in_re, in_im, out_re, out_im,
                                                                      tw, nfft, scale);
   return cudaGetLastError();
@@ -322,6 +338,7 @@ cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, 
   int64_t grid = (total2 + 255) / 256;
   if (grid > 148 * 32) grid = 148 * 32;
   if (grid < 1) grid = 1;
+  clear_stale_error();
   block_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>((const float4*)in, (float4*)out, nblocks,
                                                           rows, bw / 2, in_block_stride / 2,
                                                           out_ld / 2);
@@ -371,6 +388,7 @@ cudaError_t launch_peer_block_gather(const PeerPtrs& src, float2* out, int nrank
   int64_t grid = (total2 + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
   if (grid < 1) grid = 1;
+  clear_stale_error();
   peer_block_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>(src, (float4*)out, nranks, rows,
                                                                b / 2, out_ld / 2);
   return cudaGetLastError();
@@ -380,6 +398,7 @@ cudaError_t launch_dist_barrier(const PeerFlags& flags, int rank, int nranks, ui
                                 uint64_t timeout_ns, int* err, cudaStream_t stream) {
   if (nranks < 1 || nranks > kMaxPeers || rank < 0 || rank >= nranks || err == nullptr)
     return cudaErrorInvalidValue;
+  clear_stale_error();
   dist_barrier_kernel<<<1, 32, 0, stream>>>(flags, rank, nranks, epoch, timeout_ns, err);
   return cudaGetLastError();
 }
@@ -387,6 +406,7 @@ cudaError_t launch_dist_barrier(const PeerFlags& flags, int rank, int nranks, ui
 cudaError_t launch_cmul_interleaved(const float2* a, const float2* b, float2* out, int64_t n,
                                     cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
+  clear_stale_error();
   cmul_interleaved_kernel<<<elementwise_grid(n), 256, 0, stream>>>(a, b, out, n);
   return cudaGetLastError();
 }
@@ -395,6 +415,7 @@ cudaError_t launch_cmul_split(const float* a_re, const float* a_im, const float*
                               const float* b_im, float* o_re, float* o_im, int64_t n,
                               cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
+  clear_stale_error();
   cmul_split_kernel<<<elementwise_grid(n), 256, 0, stream>>>(a_re, a_im, b_re, b_im, o_re, o_im, n);
   return cudaGetLastError();
 }
@@ -402,6 +423,7 @@ cudaError_t launch_cmul_split(const float* a_re, const float* a_im, const float*
 cudaError_t launch_deinterleave(const float2* in, float* re, float* im, int64_t n,
                                 cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
+  clear_stale_error();
   deinterleave_kernel<<<elementwise_grid(n), 256, 0, stream>>>(in, re, im, n);
   return cudaGetLastError();
 }
@@ -409,6 +431,7 @@ cudaError_t launch_deinterleave(const float2* in, float* re, float* im, int64_t 
 cudaError_t launch_interleave(const float* re, const float* im, float2* out, int64_t n,
                               cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
+  clear_stale_error();
   interleave_kernel<<<elementwise_grid(n), 256, 0, stream>>>(re, im, out, n);
   return cudaGetLastError();
 }

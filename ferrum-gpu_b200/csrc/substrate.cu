@@ -42,7 +42,10 @@ ferrum_status ferrum_buffer_alloc_zeros(ferrum_device* dev, size_t bytes, void**
   if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, bytes);
-  if (e != cudaSuccess) return cuda_error(e, "buffer_alloc_zeros: cudaMalloc");
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return cuda_error(e, "buffer_alloc_zeros: cudaMalloc");
+  }
   e = cudaMemset(p, 0, bytes);
   if (e != cudaSuccess) {
     cudaFree(p);
@@ -91,7 +94,10 @@ ferrum_status ferrum_module_load(ferrum_device* dev, const void* image, ferrum_m
   if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
   cudaLibrary_t lib = nullptr;
   cudaError_t e = cudaLibraryLoadData(&lib, image, nullptr, nullptr, 0, nullptr, nullptr, 0);
-  if (e != cudaSuccess) return cuda_error(e, "module_load: cudaLibraryLoadData");
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // reported here; not left for a later call to find
+    return cuda_error(e, "module_load: cudaLibraryLoadData");
+  }
   auto* m = new ferrum_module();
   m->dev = dev;
   m->lib = lib;
@@ -116,8 +122,10 @@ ferrum_status ferrum_module_kernel(ferrum_module* module, const char* name, void
   DeviceGuard guard(module->dev->ordinal);
   cudaKernel_t k = nullptr;
   cudaError_t e = cudaLibraryGetKernel(&k, module->lib, name);
-  if (e != cudaSuccess)
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // reported here; not left for a later call to find
     return cuda_error(e, (std::string("module_kernel: no kernel named ") + name).c_str());
+  }
   *kernel_out = reinterpret_cast<void*>(k);
   return FERRUM_OK;
 }
@@ -134,6 +142,7 @@ ferrum_status ferrum_launch(ferrum_device* dev, void* kernel, const unsigned gri
       return set_error(FERRUM_ERR_INVALID_ARG, "launch: grid and block dimensions must be >= 1");
   DeviceGuard guard(dev->ordinal);
   if (guard.status() != cudaSuccess) return cuda_error(guard.status(), "cudaSetDevice");
+  (void)cudaGetLastError();  // an earlier unrelated error is not this launch's
   cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(kernel),
                                    dim3(grid[0], grid[1], grid[2]),
                                    dim3(block[0], block[1], block[2]), args, shared_bytes,
