@@ -235,15 +235,19 @@ def test_host_pointer_path(capi, dev, oracle_mod, log_n, batch):
     assert np.array_equal(pin_out.numpy().view(np.uint64), out.view(np.uint64))
 
 
-def test_host_pointer_2d(capi, dev, oracle_mod):
-    rng = np.random.default_rng(6100)
-    log_n, batch = 11, 5
+@pytest.mark.parametrize("log_n,batch,direction,normalize", [(11, 5, "inverse", True),
+                                                            (12, 4, "forward", False)])
+def test_host_pointer_2d(capi, dev, oracle_mod, log_n, batch, direction, normalize):
+    # N = 4096: one 128 MiB image per chunk, so the three pipeline streams run
+    # the fused column kernel concurrently, each with its own scratch slots.
+    rng = np.random.default_rng(6100 + log_n)
     n = 1 << log_n
     x = rand_c64(rng, (batch, n, n))
     out = np.empty_like(x)
-    capi.fft_2d_host(dev, x.ctypes.data, out.ctypes.data, log_n, batch, "inverse", True)
-    ref = oracle_mod.fft_2d(x[[0, 4]], log_n, "inverse", True, threads=8)
-    assert max_rel_err(out[[0, 4]], ref) < TOL
+    capi.fft_2d_host(dev, x.ctypes.data, out.ctypes.data, log_n, batch, direction, normalize)
+    pick = [0, batch - 1]
+    ref = oracle_mod.fft_2d(x[pick], log_n, direction, normalize, threads=8)
+    assert max_rel_err(out[pick], ref) < TOL
 
 
 @pytest.mark.parametrize("log_n,batch", [(8, 1 << 20), (10, 1 << 18), (12, 1 << 16), (14, 1 << 14)])
