@@ -23,7 +23,9 @@
 //
 // The host-side name of a __device__ array is not a device address, so the
 // first call on each device looks the address up with cudaGetSymbolAddress
-// while that device is current, and caches it.
+// while that device is current, and caches it. That set-up happens inside
+// the first call, so the first call on a device should come before any
+// stream capture.
 #include <cuda_runtime.h>
 
 #include <mutex>

@@ -96,7 +96,8 @@ ferrum_status ferrum_fft_1d_c2c_pow2_ws(ferrum_device *dev, const void *in_dev, 
  * library keeps that array until exit. The array is shared by all calls on a
  * device: calls that overlap on the GPU race, and none needs it zeroed. The
  * first call on each device looks up the array's device address
- * (cudaGetSymbolAddress) and caches it. */
+ * (cudaGetSymbolAddress) and caches it; make that first call on a device
+ * before any stream capture. */
 ferrum_status ferrum_fft_1d_c2c_pow2_noalloc(ferrum_device *dev, const void *in_dev,
                                              void *out_dev, int log_n, size_t batch,
                                              int direction, int normalize, void *stream);
