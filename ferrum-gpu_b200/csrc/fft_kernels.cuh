@@ -455,29 +455,35 @@ fft_rows_t_kernel(const float2* in, float2* out, const float2* __restrict__ tw, 
     for (int m = 0; m < G::P; ++m) v[m] = make_float2(0.f, 0.f);
   }
   float2* sm = smem + g * C::RS;
-  if constexpr (G::T <= 32)
-    run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
-  else
-    run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncBlock{});
-
-  // Transpose FPB rows through shared memory so that lanes run over rows.
-  __syncthreads();
-#pragma unroll
-  for (int m = 0; m < G::P; ++m) sm[stage_read_addr<LOGN, LOGP>(t, m)] = v[m];
-  __syncthreads();
+  // The store runs with lanes over rows: thread (g2, e0) ends with outputs
+  // e0 + T*q of row g2, so FPB adjacent rows give FPB-value output segments.
   const int g2 = threadIdx.x % FPB;
   const int e0 = threadIdx.x / FPB;
+  float2* row = smem + g2 * C::RS;
+  if constexpr (G::STAGES >= 2) {
+    // The last stage reads its inputs in the lanes-over-rows arrangement
+    // (one block barrier, as every row's region is read by other warps).
+    if constexpr (G::T <= 32)
+      run_stages_regroup<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{}, row, e0, SyncBlock{});
+    else
+      run_stages_regroup<LOGN, LOGP, 0>(v, sm, t, tw, SyncBlock{}, row, e0, SyncBlock{});
+  } else {
+    // One stage, no exchange: transpose through shared memory.
+    run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
+#pragma unroll
+    for (int m = 0; m < G::P; ++m) sm[stage_read_addr<LOGN, LOGP>(t, m)] = v[m];
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < G::P; ++q) v[q] = row[stage_read_addr<LOGN, LOGP>(e0, q)];
+  }
   const int64_t f2 = (int64_t)blockIdx.x * FPB + g2;
   if (f2 < a.nfft) {
     int64_t o, j, c;
     pass_index(f2, a.log_w, a.log_j, o, j, c);
     float2* dst = out + o * a.out_o + j * a.out_j + c;
-    const float2* row = smem + g2 * C::RS;
 #pragma unroll
-    for (int q = 0; q < G::P; ++q) {
-      const int e = e0 + G::T * q;
-      st_stream(dst + a.out_e * e, epilogue<CONJ_OUT>(row[stage_read_addr<LOGN, LOGP>(e0, q)], a.scale));
-    }
+    for (int q = 0; q < G::P; ++q)
+      st_stream(dst + a.out_e * (e0 + G::T * q), epilogue<CONJ_OUT>(v[q], a.scale));
   }
 }
 

@@ -280,6 +280,42 @@ __device__ __forceinline__ void run_stages(float2 (&v)[1 << LOGP], float2* sm, i
     run_stages<LOGN, LOGP, S + 1>(v, sm, t, tw, sync, after_last_read);
   }
 }
+
+// As run_stages, but the last stage runs in another thread arrangement: its
+// inputs are read by thread t_last from region sm_last (which may belong to
+// another group of the CTA), after `last_sync`, which must order the writes
+// of every group whose region that can be. On return v[m] = X[t_last + T*m] of
+// sm_last's transform. A stage's butterflies depend on the thread only through
+// the position t it reads, so the values are those run_stages gives thread
+// t_last of that group; the regrouping replaces a separate transpose exchange.
+template <int LOGN, int LOGP, int S, class Sync, class LastSync>
+__device__ __forceinline__ void run_stages_regroup(float2 (&v)[1 << LOGP], float2* sm, int t,
+                                                   const float2* tw, Sync sync, float2* sm_last,
+                                                   int t_last, LastSync last_sync) {
+  using G = Geom<LOGN, LOGP>;
+  static_assert(G::STAGES >= 2, "regrouping needs an exchange");
+  stage_compute<LOGN, LOGP, S>(v, t, tw);
+  constexpr int LR = plan_log_radix(LOGN, LOGP, S);
+  constexpr int R = 1 << LR;
+  constexpr int B = G::P / R;
+  if constexpr (S > 0) sync();  // every read of the previous exchange is done
+#pragma unroll
+  for (int i = 0; i < B; ++i)
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      sm[stage_write_addr<LOGN, LOGP, S>(t, i, r)] = v[stage_slot<LOGN, LOGP, S>(i, r)];
+  if constexpr (S + 2 == G::STAGES) {
+    last_sync();
+#pragma unroll
+    for (int m = 0; m < G::P; ++m) v[m] = sm_last[stage_read_addr<LOGN, LOGP>(t_last, m)];
+    stage_compute<LOGN, LOGP, S + 1>(v, t_last, tw);
+  } else {
+    sync();
+#pragma unroll
+    for (int m = 0; m < G::P; ++m) v[m] = sm[stage_read_addr<LOGN, LOGP>(t, m)];
+    run_stages_regroup<LOGN, LOGP, S + 1>(v, sm, t, tw, sync, sm_last, t_last, last_sync);
+  }
+}
 #endif
 
 }  // namespace ferrum
