@@ -7,9 +7,10 @@
 //   fft_pass_kernel    FPB adjacent columns per CTA, strided elements, an
 //                      optional twiddle fused into the store (2D column
 //                      passes, column passes of the multi-pass 1D transform)
-//   fft_rows_t_kernel  FPB contiguous rows per CTA, stored transposed through
-//                      shared memory (last pass of the multi-pass 1D
-//                      transform: X[k1 + N1*k2 + ...] in natural order)
+//   fft_rows_t_kernel  FPB contiguous rows per CTA, stored transposed (the
+//                      last stage runs with lanes over the rows; last pass of
+//                      the multi-pass 1D transform: X[k1 + N1*k2 + ...] in
+//                      natural order)
 //
 // Inverse transforms use the reference's conjugation identity
 // IFFT(x) = conj(FFT(conj(x))) (crates/ferrum-gpu-fft/src/cpu.rs:106-121),
@@ -190,6 +191,7 @@ struct PassArgs {
   const float2* tw_lo;
   const float2* tw_hi;
   float scale;
+  int tw_sfu;  // with a twiddle: its factors from the SFU (kernel TW = 2), not the table
 };
 
 FERRUM_HD __forceinline__ void pass_index(int64_t f, int log_w, int log_j, int64_t& o, int64_t& j,
@@ -207,7 +209,7 @@ FERRUM_HD __forceinline__ uint32_t pass_tw_step(uint32_t c, uint32_t j, uint32_t
   return c * tc + j * tj;
 }
 
-template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW>
+template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, int TW>
 struct PassCfg {
   using G = Geom<LOGN, LOGP>;
   static constexpr int THREADS = FPB * G::T;
@@ -217,14 +219,15 @@ struct PassCfg {
 
 // One strided length-2^LOGN transform per thread group: thread t loads
 // src[(t + T*m) * in_e], runs the stages, multiplies output k = t + T*m by
-// W_M^(tw_e0 + tw_d*m) when TW, and stores dst[(t + T*m) * out_e]. With
+// W_M^(tw_e0 + tw_d*m) when TW (factors from the SFU when TW_SFU, else from
+// the two-level table), and stores dst[(t + T*m) * out_e]. With
 // LD_STREAM / ST_STREAM the data is read or written once and takes the
 // streaming (evict-first) hints; otherwise it is scratch kept in L2 between a
 // store and one later load: stores carry an L2 evict-last policy and loads an
 // evict-first one (the line is dead after it), which cut the scratch lines
 // written back to HBM.
 template <int LOGN, int LOGP, bool CONJ_IN, bool CONJ_OUT, bool TW, bool LD_STREAM, bool ST_STREAM,
-          class Sync>
+          bool TW_SFU, class Sync>
 __device__ __forceinline__ void strided_unit(const float2* src, int64_t in_e, float2* dst,
                                              int64_t out_e, bool valid, int t, float2* sm,
                                              const float2* __restrict__ tw, uint32_t tw_e0,
@@ -255,7 +258,7 @@ __device__ __forceinline__ void strided_unit(const float2* src, int64_t in_e, fl
   }
   run_stages<LOGN, LOGP, 0>(v, sm, t, tw, sync);
   if (valid) {
-    if constexpr (TW) apply_progression_twiddles<G::P>(v, tw_lo, tw_hi, tw_e0, tw_d, tw_mask);
+    if constexpr (TW) apply_progression_twiddles<G::P>(v, tw_lo, tw_hi, tw_e0, tw_d, tw_mask, TW_SFU);
     dst += (int64_t)t * out_e;
     const int64_t step = (int64_t)G::T * out_e;
 #pragma unroll
@@ -273,7 +276,8 @@ __device__ __forceinline__ void strided_unit(const float2* src, int64_t in_e, fl
   }
 }
 
-template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, bool TW>
+// TW: 0 no twiddle, 1 twiddle factors from the table, 2 from the SFU.
+template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT, int TW>
 __global__ void __launch_bounds__(PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS,
                                   MinBlocks<PassCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT, TW>::THREADS, LOGP>::value)
 fft_pass_kernel(const float2* in, float2* out, const float2* __restrict__ tw, PassArgs a) {
@@ -294,11 +298,11 @@ fft_pass_kernel(const float2* in, float2* out, const float2* __restrict__ tw, Pa
   const float2* src = in + o * a.in_o + j * a.in_j + c * a.in_c;
   float2* dst = out + o * a.out_o + j * a.out_j + c * a.out_c;
   if constexpr (FPB == 1 && G::T <= 32)
-    strided_unit<LOGN, LOGP, CONJ_IN, CONJ_OUT, TW, true, true>(
+    strided_unit<LOGN, LOGP, CONJ_IN, CONJ_OUT, TW != 0, true, true, TW == 2>(
         src, a.in_e, dst, a.out_e, valid, t, sm, tw, tb + ts * (uint32_t)t, ts * (uint32_t)G::T,
         a.tw_lo, a.tw_hi, mask, a.scale, SyncWarp{});
   else
-    strided_unit<LOGN, LOGP, CONJ_IN, CONJ_OUT, TW, true, true>(
+    strided_unit<LOGN, LOGP, CONJ_IN, CONJ_OUT, TW != 0, true, true, TW == 2>(
         src, a.in_e, dst, a.out_e, valid, t, sm, tw, tb + ts * (uint32_t)t, ts * (uint32_t)G::T,
         a.tw_lo, a.tw_hi, mask, a.scale, SyncBlock{});
 }
@@ -378,7 +382,7 @@ fft_cols_l2_kernel(const float2* in, float2* out, float2* ws, const float2* __re
         // registers across rounds (which spilled at 64 registers).
         const float2* twr = tw1;
         asm volatile("" : "+l"(twr));
-        strided_unit<L1, C::LP1, CONJ_IN, false, true, true, false>(
+        strided_unit<L1, C::LP1, CONJ_IN, false, true, true, false, false>(
             in + base + j * a.ld, (int64_t)A * a.ld, slot + j * W + cl, (int64_t)A * W, true, t1,
             sm1, twr, (uint32_t)j * (uint32_t)t1, (uint32_t)j * (uint32_t)C::G1::T, a.tw_lo,
             a.tw_hi, kMask, 1.0f, sync1);
@@ -397,7 +401,7 @@ fft_cols_l2_kernel(const float2* in, float2* out, float2* ws, const float2* __re
         const int j = r * C::U2 + u2;  // kb
         const float2* twr = tw2;
         asm volatile("" : "+l"(twr));
-        strided_unit<L2, C::LP2, false, CONJ_OUT, false, false, true>(
+        strided_unit<L2, C::LP2, false, CONJ_OUT, false, false, true, false>(
             slot + (int64_t)A * j * W + cl, (int64_t)W, out + base + j * a.ld, (int64_t)B * a.ld,
             true, t2, sm2, twr, 0u, 0u, nullptr, nullptr, 0u, a.scale, sync2);
         sync2();

@@ -147,7 +147,7 @@ cudaError_t rows_pf_impl(const float2* in, float2* out, const float2* tw, int64_
   return cudaGetLastError();
 }
 
-template <int LOGN, bool CI, bool CO, bool TW>
+template <int LOGN, bool CI, bool CO, int TW>
 cudaError_t pass_impl(const float2* in, float2* out, const float2* tw, const PassArgs& a,
                       cudaStream_t s) {
   constexpr int LOGP = plan_log_p(LOGN);
@@ -239,13 +239,20 @@ template <int LOGN>
 cudaError_t pass_dispatch(bool ci, bool co, bool tw, const float2* in, float2* out,
                           const float2* stw, const PassArgs& a, cudaStream_t s) {
   if (!pass_flags_supported(ci, co, tw)) return cudaErrorInvalidValue;
-  if (tw) {
-    if (ci) return pass_impl<LOGN, true, false, true>(in, out, stw, a, s);
-    return pass_impl<LOGN, false, false, true>(in, out, stw, a, s);
+  if (tw && a.tw_sfu) {
+    if constexpr (pass_sfu_supported(LOGN)) {
+      if (ci) return pass_impl<LOGN, true, false, 2>(in, out, stw, a, s);
+      return pass_impl<LOGN, false, false, 2>(in, out, stw, a, s);
+    }
+    return cudaErrorInvalidValue;
   }
-  if (ci) return pass_impl<LOGN, true, false, false>(in, out, stw, a, s);
-  if (co) return pass_impl<LOGN, false, true, false>(in, out, stw, a, s);
-  return pass_impl<LOGN, false, false, false>(in, out, stw, a, s);
+  if (tw) {
+    if (ci) return pass_impl<LOGN, true, false, 1>(in, out, stw, a, s);
+    return pass_impl<LOGN, false, false, 1>(in, out, stw, a, s);
+  }
+  if (ci) return pass_impl<LOGN, true, false, 0>(in, out, stw, a, s);
+  if (co) return pass_impl<LOGN, false, true, 0>(in, out, stw, a, s);
+  return pass_impl<LOGN, false, false, 0>(in, out, stw, a, s);
 }
 
 template <int LOGN>

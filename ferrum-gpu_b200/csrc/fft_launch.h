@@ -33,7 +33,9 @@ cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, 
 // Strided pass (fft_pass_kernel) of length 2^log_n, 2 <= log_n <= 14; with
 // tw the twiddle described by the PassArgs is fused into the store. The
 // (conj_in, conj_out, tw) combinations are those pass_flags_supported()
-// (passes.h) accepts; others return cudaErrorInvalidValue.
+// (passes.h) accepts; others return cudaErrorInvalidValue. With tw,
+// args.tw_sfu selects the kernel that takes the twiddle factors from the SFU
+// instead of the two-level table.
 cudaError_t launch_pass(int log_n, bool conj_in, bool conj_out, bool tw, const float2* in,
                         float2* out, const float2* stage_tw, const PassArgs& args,
                         cudaStream_t stream);

@@ -66,6 +66,10 @@ constexpr bool pass_flags_supported(bool ci, bool co, bool tw) {
   return tw ? !co : !(ci && co);
 }
 
+// Pass lengths compiled with SFU twiddle factors (the column passes of the
+// multi-pass 1D transform, 2^15..2^26, have lengths 2^7..2^10).
+constexpr bool pass_sfu_supported(int log_n) { return log_n >= 7 && log_n <= 10; }
+
 inline PassDesc make_rows(int log_n, int64_t nfft, bool ci, bool co, float scale, PassBuf src,
                           PassBuf dst, int log_block = -1, int64_t block_rows = 0) {
   PassDesc d{};
@@ -184,6 +188,7 @@ inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
     PassArgs a = pass_args(batch * n2, l2, 0, n, 0, n2, n, 0, n2);
     a.tc = 1;
     a.log_m = log_n;
+    a.tw_sfu = pass_sfu_supported(l1);
     pl.p[pl.count++] = make_pass(l1, inv, false, PassBuf::In, PassBuf::Ws, a);
     RowsTArgs b{};
     b.nfft = batch * n1;
@@ -203,11 +208,13 @@ inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
   PassArgs a1 = pass_args(batch * n2 * n3, l3, l2, n, n3, n2 * n3, n, n3, n2 * n3);
   a1.tj = 1;
   a1.log_m = l1 + l2;
+  a1.tw_sfu = pass_sfu_supported(l1);
   pl.p[pl.count++] = make_pass(l1, inv, false, PassBuf::In, PassBuf::Ws, a1);
   PassArgs a2 = pass_args(batch * n1 * n3, l3, l1, n, n2 * n3, n3, n, n2 * n3, n3);
   a2.tcj = 1;
   a2.tc = (uint32_t)n1;
   a2.log_m = log_n;
+  a2.tw_sfu = pass_sfu_supported(l2);
   pl.p[pl.count++] = make_pass(l2, false, false, PassBuf::Ws, PassBuf::Ws, a2);
   RowsTArgs b{};
   b.nfft = batch * n1 * n2;

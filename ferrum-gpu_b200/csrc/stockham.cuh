@@ -209,36 +209,75 @@ FERRUM_HD __forceinline__ float2 four_step_twiddle(const float2* lo, const float
                tw_load(lo + (e & ((1u << kFourStepLoBits) - 1))));
 }
 
-// v[m] *= W_M^(e0 + d*m) for m < P (M = mask + 1, a power of two): the
-// twiddles of one thread's outputs k = t + T*m in a strided pass, whose
-// exponents form an arithmetic progression. W_M^e0 and W_M^(d*2^b) come from
-// the two-level table (1 + log2 P lookups instead of P); W_M^(e0 + d*m) is
-// their product over the set bits b of m, at most 1 + log2 P correctly rounded
-// factors. The lookups are what the lanes of a warp gather from scattered
-// addresses, so cutting them relieves the L1 pipe.
-template <int P>
-FERRUM_HD __forceinline__ void apply_progression_twiddles(float2 (&v)[P], const float2* lo,
-                                                          const float2* hi, uint32_t e0,
-                                                          uint32_t d, uint32_t mask) {
+// v[m] *= W_M^(e0 + d*m) for m < P, with W_M^e0 and W_M^(d*2^b) from
+// `factor` (1 + log2 P evaluations instead of P): W_M^(e0 + d*m) is their
+// product over the set bits b of m, at most 1 + log2 P factors.
+template <int P, class Factor>
+FERRUM_HD __forceinline__ void progression_twiddles_by(float2 (&v)[P], uint32_t e0, uint32_t d,
+                                                       Factor factor) {
   constexpr int H = P / 2;
   float2 w[H > 0 ? H : 1];
-  w[0] = four_step_twiddle(lo, hi, e0 & mask);
+  w[0] = factor(e0);
   if constexpr (P == 1) {
     v[0] = c_mul(v[0], w[0]);
   } else {
 #pragma unroll
     for (int b = 1; b < H; b <<= 1) {
-      const float2 p = four_step_twiddle(lo, hi, (d * (uint32_t)b) & mask);
+      const float2 p = factor(d * (uint32_t)b);
 #pragma unroll
       for (int m = 0; m < b; ++m) w[m + b] = c_mul(w[m], p);
     }
-    const float2 top = four_step_twiddle(lo, hi, (d * (uint32_t)H) & mask);
+    const float2 top = factor(d * (uint32_t)H);
 #pragma unroll
     for (int m = 0; m < H; ++m) {
       v[m + H] = c_mul(v[m + H], c_mul(w[m], top));
       v[m] = c_mul(v[m], w[m]);
     }
   }
+}
+
+#if defined(__CUDACC__)
+// W_M^e, M = 2^(32 - sh), from the special-function unit: e << sh is the
+// exponent as a signed 32-bit fixed-point fraction of a turn, so the angle
+// -2*pi*e/M is taken in [-pi, pi), where __sinf / __cosf are within 2^-21.4
+// absolute; with the rounding of the integer-to-float conversion and of the
+// scaling each component is within ~7e-7 of exp(-2*pi*i*e/M) (a correctly
+// rounded table entry: ~6e-8).
+__device__ __forceinline__ float2 sfu_twiddle(uint32_t e, int sh) {
+  float s, c;
+  __sincosf((float)(int32_t)(e << sh) * -1.46291808e-9f, &s, &c);  // -2*pi / 2^32
+  return make_float2(c, s);
+}
+#endif
+
+// v[m] *= W_M^(e0 + d*m) for m < P (M = mask + 1, a power of two, M >= 2):
+// the twiddles of one thread's outputs k = t + T*m in a strided pass, whose
+// exponents form an arithmetic progression. The factors come from the
+// two-level table (two lookups each), or, with `sfu` on the device, from the
+// special-function unit. The passes of the multi-pass 1D transform take the
+// SFU path: the lookups of their four-step twiddles filled the L1 data pipe
+// (lanes of different columns gather from different cache lines), and the
+// SFU factors measured faster for every length (1D 2^18 x 1024: 1.83 ->
+// 1.66 ms, 2^24 x 4: 0.597 -> 0.581 ms per transform). The 2D column
+// sub-passes keep the table, where they measured faster (their twiddle
+// W_N^(a*kb) is the same for all columns, so the lanes of a warp share the
+// entries). The host (CPU emulator) always uses the table.
+template <int P>
+FERRUM_HD __forceinline__ void apply_progression_twiddles(float2 (&v)[P], const float2* lo,
+                                                          const float2* hi, uint32_t e0,
+                                                          uint32_t d, uint32_t mask,
+                                                          bool sfu = false) {
+#if defined(__CUDA_ARCH__)
+  if (sfu) {
+    const int sh = __clz(mask);
+    progression_twiddles_by(v, e0, d, [sh](uint32_t e) { return sfu_twiddle(e, sh); });
+    return;
+  }
+#else
+  (void)sfu;
+#endif
+  progression_twiddles_by(v, e0, d,
+                          [lo, hi, mask](uint32_t e) { return four_step_twiddle(lo, hi, e & mask); });
 }
 
 // Blocked layout of the distributed row pass: element e of row f (of nrows)

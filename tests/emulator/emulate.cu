@@ -206,6 +206,7 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst, float2* ws) {
     case PassKind::Pass: {
       const PassArgs& a = d.pa;
       if (!pass_flags_supported(d.conj_in, d.conj_out, a.log_m > 0)) return -60;
+      if (a.tw_sfu && (a.log_m == 0 || !pass_sfu_supported(d.log_n))) return -62;
       const uint32_t mask = a.log_m > 0 ? (1u << a.log_m) - 1u : 0u;
       for (int64_t f = 0; f < a.nfft; ++f) {
         int64_t o, j, c;
