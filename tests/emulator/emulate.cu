@@ -5,7 +5,9 @@
 // kernels: the radix plans (plan.h), the twiddle tables the runtime uploads
 // (twiddle_tables.h), stage_compute / stage_out_pos / stage_slot / smem_pad
 // (stockham.cuh), pass_index / pass_tw_base / pass_tw_step and the two-level
-// twiddle lookup (fft_kernels.cuh), and the distributed blocked layout. Each
+// twiddle lookup (fft_kernels.cuh), and the distributed blocked layout (the
+// device takes the multi-pass 1D twiddle factors from the SFU instead of the
+// table; the emulator checks that those passes have a compiled length). Each
 // thread group is simulated thread by thread between barriers, and every
 // shared-memory exchange is checked to be a permutation (each padded slot
 // written exactly once and read exactly once). The tests compare its output
