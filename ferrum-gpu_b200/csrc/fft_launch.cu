@@ -31,14 +31,19 @@ constexpr int rows_fpb(int log_n) {
              ? kRowsThreads / (1 << (log_n - plan_log_p(log_n)))
              : 1;
 }
-constexpr int cols_fpb(int log_n) {
-  // clamp(512 / T, 1, 16)
-  return (kColsThreads >> (log_n - plan_log_p(log_n))) < 1
+constexpr int cols_fpb(int log_n, int threads = kColsThreads) {
+  // clamp(threads / T, 1, 16)
+  return (threads >> (log_n - plan_log_p(log_n))) < 1
              ? 1
-             : ((kColsThreads >> (log_n - plan_log_p(log_n))) > 16
+             : ((threads >> (log_n - plan_log_p(log_n))) > 16
                     ? 16
-                    : (kColsThreads >> (log_n - plan_log_p(log_n))));
+                    : (threads >> (log_n - plan_log_p(log_n))));
 }
+// The SFU-twiddle column passes of the multi-pass 1D transform are latency-
+// bound (their block barriers keep a CTA's warps in step); 256-thread CTAs,
+// more of them per SM and out of step, measured 2-3 % faster at 2^18 and 2^19
+// and level elsewhere, although N1 = 1024 then reads 32-byte row segments.
+constexpr int kSfuColsThreads = 256;
 
 // Raise the dynamic shared-memory limit once per (kernel, device). `done` is
 // a per-instantiation flag word owned by the caller (one bit per device).
@@ -151,7 +156,7 @@ template <int LOGN, bool CI, bool CO, int TW>
 cudaError_t pass_impl(const float2* in, float2* out, const float2* tw, const PassArgs& a,
                       cudaStream_t s) {
   constexpr int LOGP = plan_log_p(LOGN);
-  constexpr int FPB = cols_fpb(LOGN);
+  constexpr int FPB = cols_fpb(LOGN, TW == 2 ? kSfuColsThreads : kColsThreads);
   using C = PassCfg<LOGN, LOGP, FPB, CI, CO, TW>;
   auto k = fft_pass_kernel<LOGN, LOGP, FPB, CI, CO, TW>;
   static std::atomic<uint64_t> smem_done{0};
