@@ -467,8 +467,12 @@ fft_rows_t_kernel(const float2* in, float2* out, const float2* __restrict__ tw, 
   if constexpr (G::STAGES >= 2) {
     // The last stage reads its inputs in the lanes-over-rows arrangement
     // (one block barrier, as every row's region is read by other warps).
+    // The exchanges before it stay within the row's own warps (a named
+    // barrier per row when a row spans several warps).
     if constexpr (G::T <= 32)
       run_stages_regroup<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{}, row, e0, SyncBlock{});
+    else if constexpr (FPB > 1 && FPB <= 15)
+      run_stages_regroup<LOGN, LOGP, 0>(v, sm, t, tw, SyncNamed{1 + g, G::T}, row, e0, SyncBlock{});
     else
       run_stages_regroup<LOGN, LOGP, 0>(v, sm, t, tw, SyncBlock{}, row, e0, SyncBlock{});
   } else {
