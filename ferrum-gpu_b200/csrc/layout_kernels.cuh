@@ -71,6 +71,8 @@ fft_rows_split_kernel(const float* __restrict__ in_re, const float* __restrict__
     }
     if constexpr (G::T <= 32)
       run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
+    else if constexpr (FPB > 1 && FPB <= 15)
+      run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncNamed{1 + g, G::T});
     else
       run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncBlock{});
     if (valid) {
