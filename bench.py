@@ -343,12 +343,32 @@ def _time_ms(fn, stream, reps: int = 5, warm: int = 2) -> float:
     return a.elapsed_time(b) / reps
 
 
+def _cufft_fns(x, y, batch: int, log_n: int, kind: str):
+    """Forward and inverse (1/N) cuFFT calls through torch.fft on the same
+    device buffers: the reference's yardstick (its bench states every result
+    as a ratio to cuFFT on identical buffers), never part of the product."""
+    import torch
+
+    n = 1 << log_n
+    if kind == "1d":
+        xv = x[: batch * n].view(batch, n)
+        yv = y[: batch * n].view(batch, n)
+        return (lambda: torch.fft.fft(xv, dim=-1, out=yv),
+                lambda: torch.fft.ifft(yv, dim=-1, out=xv))
+    xv = x[: batch * n * n].view(batch, n, n)
+    yv = y[: batch * n * n].view(batch, n, n)
+    return (lambda: torch.fft.fft2(xv, out=yv), lambda: torch.fft.ifft2(yv, out=xv))
+
+
 def measure_extras(capi, dev, x, y, world, rank, barrier, max_over_ranks) -> dict:
     """Secondary measurements on the same device buffers (2^28 complex each):
-    the other sweep sizes, the large-N four-step sizes, 2D 4096^2 x 16 and the
-    16384^2 2D transform (single GPU at N=1, distributed over NCCL at N>1).
-    GB/s count 16 B per element per pass (1 pass for N <= 2^14, 2 for the
-    four-step and 2D)."""
+    BASELINE config 1 (N=1024 x 256, L2-resident), the sweep sizes, the
+    large-N multi-pass sizes, 2D 4096^2 x 16 and the 16384^2 2D transform
+    (single GPU at N=1, distributed at N>1), each forward and inverse (1/N),
+    with cuFFT on the same buffers as a yardstick (`cufft_*_ms`,
+    `vs_cufft` = cuFFT time / ours, > 1 when ours is faster). GB/s count 16 B
+    per element per pass (1 pass for N <= 2^14, 2 for the multi-pass 1D and
+    2D). The inputs of every timed config except config 1 exceed the L2."""
     import torch
 
     stream = torch.cuda.current_stream()
@@ -359,49 +379,75 @@ def measure_extras(capi, dev, x, y, world, rank, barrier, max_over_ranks) -> dic
     def gbs(passes, elems, ms):
         return round(world * passes * 16 * elems / (ms * 1e-3) / 1e9, 1)
 
+    def one(key, log_n, batch, kind, reps=5, cufft=True):
+        fft = capi.fft_1d if kind == "1d" else capi.fft_2d
+        elems = batch << (log_n * (2 if kind == "2d" else 1))
+        passes = passes_counted(kind, log_n)
+        ms_f = max_over_ranks(_time_ms(lambda: fft(dev, x.data_ptr(), y.data_ptr(), log_n, batch,
+                                                   "forward", False, sp), stream, reps))
+        ms_i = max_over_ranks(_time_ms(lambda: fft(dev, y.data_ptr(), x.data_ptr(), log_n, batch,
+                                                   "inverse", True, sp), stream, reps))
+        rec = {"ms": round(ms_f, 4), "GB/s": gbs(passes, elems, ms_f),
+               "inverse_ms": round(ms_i, 4), "inverse_GB/s": gbs(passes, elems, ms_i)}
+        if cufft:
+            cf, ci = _cufft_fns(x, y, batch, log_n, kind)
+            try:
+                c_f = max_over_ranks(_time_ms(cf, stream, reps))
+                c_i = max_over_ranks(_time_ms(ci, stream, reps))
+                rec.update({"cufft_ms": round(c_f, 4), "cufft_inverse_ms": round(c_i, 4),
+                            "vs_cufft": round(c_f / ms_f, 3),
+                            "vs_cufft_inverse": round(c_i / ms_i, 3)})
+            except Exception as e:  # yardstick only: never fail the bench over it
+                rec["cufft"] = f"unavailable: {type(e).__name__}: {e}"
+            # cuFFT's inverse wrote x: restore a well-scaled input for the next config
+            torch.cuda.synchronize()
+        out[key] = rec
+
+    one("config1_1d_N1024_x256_L2_resident", 10, 256, "1d", reps=200)
     for log_n in (8, 10, 12, 14):
-        batch = total >> log_n
-        ms = max_over_ranks(_time_ms(lambda: capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), log_n,
-                                                         batch, "forward", False, sp), stream))
-        out[f"1d_N{1 << log_n}_x{batch}_fwd"] = {"GB/s": gbs(1, total, ms), "ms": round(ms, 4)}
+        one(f"1d_N{1 << log_n}_x{total >> log_n}", log_n, total >> log_n, "1d")
     for log_n, batch in ((20, 64), (24, 4)):
-        ms = max_over_ranks(_time_ms(lambda: capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), log_n,
-                                                         batch, "forward", False, sp), stream))
-        out[f"1d_N2^{log_n}_x{batch}_fwd"] = {"GB/s": gbs(2, batch << log_n, ms), "ms": round(ms, 4)}
-    ms = max_over_ranks(_time_ms(lambda: capi.fft_2d(dev, x.data_ptr(), y.data_ptr(), 12, 16,
-                                                     "forward", False, sp), stream))
-    out["2d_4096^2_x16_fwd"] = {"GB/s": gbs(2, 16 << 24, ms), "ms": round(ms, 4)}
+        one(f"1d_N2^{log_n}_x{batch}", log_n, batch, "1d")
+    one("2d_4096^2_x16", 12, 16, "2d")
 
     n = 1 << 14
     if world == 1:
-        ms = _time_ms(lambda: capi.fft_2d(dev, x.data_ptr(), y.data_ptr(), 14, 1, "forward", False,
-                                          sp), stream)
-        capi.fft_2d(dev, y.data_ptr(), y.data_ptr(), 14, 1, "inverse", True, sp)
+        one("2d_16384^2", 14, 1, "2d")
+        capi.fft_2d(dev, x.data_ptr(), y.data_ptr(), 14, 1, "forward", False, sp)
+        z = torch.empty(n * n, dtype=x.dtype, device=x.device)
+        capi.fft_2d(dev, y.data_ptr(), z.data_ptr(), 14, 1, "inverse", True, sp)
         torch.cuda.synchronize()
-        err = float((y - x).abs().max() / x.abs().max())
-        out["2d_16384^2_fwd"] = {"ms": round(ms, 4), "GB/s": gbs(2, n * n, ms),
-                                 "path": "single GPU (row pass + column pass)",
-                                 "roundtrip_max_rel_err": err}
+        xs = x[: n * n]
+        out["2d_16384^2"]["path"] = "single GPU (column passes + row pass)"
+        out["2d_16384^2"]["roundtrip_max_rel_err"] = float((z - xs).abs().max() / xs.abs().max())
+        del z
     else:
         from ferrum_gpu.dist import Dist2D
 
-        ctx = Dist2D(dev, timeout_ms=120000)
+        # Set-up (slab allocation, IPC mapping) happens in the first call,
+        # under a generous bound; the timed calls' peer barriers then give up
+        # after 5 s instead of spinning on a lost peer.
+        ctx = Dist2D(dev, timeout_ms=60000)
         rows = n // world
         xs = x[: rows * n]
         ys = y[: rows * n]
         zs = torch.empty_like(xs)
         barrier()
+        ctx.fft_2d(xs.data_ptr(), ys.data_ptr(), 14, "forward", False, sp, "rows", "cols")
+        ctx.sync(sp)
+        ctx.set_timeout(5000)
+        barrier()
         # Forward: row slabs -> column slabs (row FFTs, one all-to-all
         # exchange, column FFTs); inverse: column slabs -> row slabs.
         ms_f = max_over_ranks(_time_ms(lambda: ctx.fft_2d(xs.data_ptr(), ys.data_ptr(), 14,
                                                           "forward", False, sp, "rows", "cols"),
-                                       stream))
+                                       stream, 20))
         ms_i = max_over_ranks(_time_ms(lambda: ctx.fft_2d(ys.data_ptr(), zs.data_ptr(), 14,
                                                           "inverse", True, sp, "cols", "rows"),
-                                       stream))
+                                       stream, 20))
         ms_rr = max_over_ranks(_time_ms(lambda: ctx.fft_2d(xs.data_ptr(), ys.data_ptr(), 14,
                                                            "forward", False, sp, "rows", "rows"),
-                                        stream))
+                                        stream, 20))
         ctx.fft_2d(xs.data_ptr(), ys.data_ptr(), 14, "forward", False, sp, "rows", "cols")
         ctx.fft_2d(ys.data_ptr(), zs.data_ptr(), 14, "inverse", True, sp, "cols", "rows")
         ctx.sync(sp)
@@ -410,16 +456,52 @@ def measure_extras(capi, dev, x, y, world, rank, barrier, max_over_ranks) -> dic
         peer = ctx.peer_path == 1
         ctx.close()
         slab_bytes = rows * n * 8
-        out["2d_16384^2_fwd"] = {"ms": round(ms_f, 4), "inverse_ms": round(ms_i, 4),
-                                 "rows_to_rows_fwd_ms": round(ms_rr, 4),
-                                 "data_path": "peer memory (exchange fused into the FFT kernels)"
-                                 if peer else "NCCL send/recv",
-                                 "nvlink_bytes_per_rank_each_way": (world - 1) * slab_bytes // world,
-                                 "path": f"distributed over {world} GPUs: row slabs -> column "
-                                         f"slabs (one all-to-all exchange); inverse column -> "
-                                         f"row slabs",
-                                 "roundtrip_max_rel_err": err}
+        out["2d_16384^2"] = {"ms": round(ms_f, 4), "inverse_ms": round(ms_i, 4),
+                             "GB/s": gbs(2, n * n // world, ms_f),
+                             "rows_to_rows_fwd_ms": round(ms_rr, 4),
+                             "data_path": "peer memory (exchange fused into the FFT kernels)"
+                             if peer else "NCCL send/recv",
+                             "nvlink_bytes_per_rank_each_way": (world - 1) * slab_bytes // world,
+                             "path": f"distributed over {world} GPUs: row slabs -> column "
+                                     f"slabs (one all-to-all exchange); inverse column -> "
+                                     f"row slabs",
+                             "roundtrip_max_rel_err": err}
     return out
+
+
+def measure_sustained(capi, dev, x, y, z, log_n, batch, local, seconds=1.2) -> dict:
+    """The headline step (forward + inverse) repeated for about `seconds` of
+    GPU time with its own clock samples: the throughput a caller running
+    FFTs for seconds sees under the 1 kW power cap."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), log_n, batch, "forward", False, sp)
+        capi.fft_1d(dev, y.data_ptr(), z.data_ptr(), log_n, batch, "inverse", True, sp)
+
+    per = _time_ms(step, stream, reps=5, warm=2)
+    steps = max(10, int(seconds * 1e3 / max(per, 1e-3)))
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    sampler.mark_begin()
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    b.synchronize()
+    sampler.mark_end()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(b)
+    elems = batch << log_n
+    return {"steps": steps, "ms_per_step": round(ms / steps, 4), "seconds": round(ms * 1e-3, 3),
+            "GB/s": round(steps * 2 * 16 * elems / (ms * 1e-3) / 1e9, 1), "clocks": clocks}
 
 
 def rows_kernel_name(log_n: int) -> str:
@@ -549,8 +631,10 @@ def run_ours(args) -> None:
 
     extras = None
     if not args.no_extras and (kind, L, B_) == ("1d", LOG_N, BATCH):
+        sustained = measure_sustained(capi, dev, x, y, z, L, B_, local)
         extras = measure_extras(capi, dev, x.view(-1), y.view(-1), world, rank, barrier,
                                 max_over_ranks)
+        extras["sustained"] = sustained
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

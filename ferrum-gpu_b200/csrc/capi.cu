@@ -76,13 +76,12 @@ ferrum_status check_device(const ferrum_device* dev) {
 }
 
 ferrum_status check_common(int log_n, int lo, int hi, size_t batch, int direction,
-                           const char* what) {
+                           const char* what, int dims = 1) {
   if (log_n < lo || log_n > hi)
     return set_error(FERRUM_ERR_INVALID_ARG, std::string(what) + ": log_n must be in [" +
                                                  std::to_string(lo) + ", " + std::to_string(hi) +
                                                  "], got " + std::to_string(log_n));
-  if (batch == 0)
-    return set_error(FERRUM_ERR_INVALID_ARG, std::string(what) + ": batch must be positive");
+  if (ferrum_status s = check_elements(dims * log_n, batch, what)) return s;
   if (!valid_direction(direction))
     return set_error(FERRUM_ERR_INVALID_ARG,
                      std::string(what) + ": direction must be +1 (forward) or -1 (inverse), got " +
@@ -93,6 +92,17 @@ ferrum_status check_common(int log_n, int lo, int hi, size_t batch, int directio
 bool is_aligned8(const void* p) { return ((uintptr_t)p & 7u) == 0; }
 
 }  // namespace
+
+ferrum_status check_elements(int elem_log, size_t batch, const char* what) {
+  if (batch == 0)
+    return set_error(FERRUM_ERR_INVALID_ARG, std::string(what) + ": batch must be positive");
+  if (elem_log > kMaxLogElems || batch > ((size_t)1 << (kMaxLogElems - elem_log)))
+    return set_error(FERRUM_ERR_INVALID_ARG,
+                     std::string(what) + ": batch " + std::to_string(batch) +
+                         " times the transform size exceeds 2^" + std::to_string(kMaxLogElems) +
+                         " complex values per call");
+  return FERRUM_OK;
+}
 
 size_t workspace_1d_bytes(int log_n, int64_t batch) {
   return (size_t)plan_1d(log_n, batch, false, false).ws_elems * sizeof(float2);
@@ -305,7 +315,7 @@ ferrum_status ferrum_fft_workspace_bytes(int log_n, size_t batch, int kind, size
     return FERRUM_OK;
   }
   if (kind == 2) {
-    if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "workspace"))
+    if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "workspace", 2))
       return s;
     *bytes = workspace_2d_bytes(log_n, (int64_t)batch);
     return FERRUM_OK;
@@ -322,7 +332,7 @@ ferrum_status ferrum_fft_launch_count(int log_n, size_t batch, int kind, int* la
     return FERRUM_OK;
   }
   if (kind == 2) {
-    if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "launch_count"))
+    if (ferrum_status s = check_common(log_n, 2, kMaxSinglePassLogN, batch, 1, "launch_count", 2))
       return s;
     *launches = plan_2d(log_n, (int64_t)batch, false, false).count;
     return FERRUM_OK;
@@ -468,7 +478,7 @@ ferrum_status ferrum_fft_2d_c2c_pow2(ferrum_device* dev, const void* in_dev, voi
   clear_error();
   if (ferrum_status s = check_device(dev)) return s;
   if (ferrum_status s =
-          check_common(log_n, 2, kMaxSinglePassLogN, batch, direction, "fft_2d_c2c_pow2"))
+          check_common(log_n, 2, kMaxSinglePassLogN, batch, direction, "fft_2d_c2c_pow2", 2))
     return s;
   if (in_dev == nullptr || out_dev == nullptr)
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2: in/out is NULL");

@@ -38,6 +38,8 @@
 // the context's timeout, after which the communicator is aborted and
 // FERRUM_ERR_TIMEOUT returned.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -395,9 +397,22 @@ ferrum_status dist_p2p(ferrum_dist_ctx* ctx, const float2* in, float2* out, int 
   PeerPtrs blocks{};
   for (int q = 0; q < ctx->nranks; ++q) blocks.p[q] = peer_slab(ctx, q) + ctx->rank * b * b;
   float2* mine = peer_slab(ctx, ctx->rank);
+  // The column passes of the local slab; their workspace (an intermediate
+  // slab, or the fused kernel's scratch slots) is sized from the plan itself.
+  PassPlan cols;
+  if (row_in)
+    plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::Ws,
+                 PassBuf::Out);
+  else
+    plan_columns(cols, log_n, lb, b, 1, n * b, inv, false, 1.0f, PassBuf::In, PassBuf::Ws,
+                 PassBuf::Out);
+  int64_t ws_elems = cols.ws_elems;
+  for (int i = 0; i < cols.count; ++i)
+    if (cols.p[i].src == PassBuf::Ws || cols.p[i].dst == PassBuf::Ws)
+      ws_elems = std::max<int64_t>(ws_elems, b * n);
   void* ws = nullptr;
-  if (log_n > kMaxOnePassColumnLogN) {
-    cudaError_t e = cudaMallocFromPoolAsync(&ws, (size_t)(b * n) * sizeof(float2), dev->pool, stream);
+  if (ws_elems > 0) {
+    cudaError_t e = cudaMallocFromPoolAsync(&ws, (size_t)ws_elems * sizeof(float2), dev->pool, stream);
     if (e != cudaSuccess) return cuda_error(e, "cudaMallocFromPoolAsync(dist workspace)");
   }
   ferrum_status s = FERRUM_OK;
@@ -407,14 +422,11 @@ ferrum_status dist_p2p(ferrum_dist_ctx* ctx, const float2* in, float2* out, int 
   };
   do {
     if ((s = p2p_barrier(ctx, stream)) != FERRUM_OK) break;
-    PassPlan cols;
     if (row_in) {
       if (!launched(launch_rows_scatter(log_n, inv, in, blocks, tw, b, lb, stream),
                     "distributed row pass (peer stores)"))
         break;
       if ((s = p2p_barrier(ctx, stream)) != FERRUM_OK) break;
-      plan_columns(cols, log_n, lb, b, 1, n * b, false, inv, scale, PassBuf::In, PassBuf::Ws,
-                   PassBuf::Out);
       if ((s = run_plan(dev, cols, mine, row_out ? mine : out, (float2*)ws, stream)) != FERRUM_OK)
         break;
       if (!row_out) break;
@@ -422,8 +434,6 @@ ferrum_status dist_p2p(ferrum_dist_ctx* ctx, const float2* in, float2* out, int 
       launched(launch_peer_block_gather(blocks, out, ctx->nranks, b, b, n, stream),
                "row-slab gather (peer loads)");
     } else {
-      plan_columns(cols, log_n, lb, b, 1, n * b, inv, false, 1.0f, PassBuf::In, PassBuf::Ws,
-                   PassBuf::Out);
       if ((s = run_plan(dev, cols, in, mine, (float2*)ws, stream)) != FERRUM_OK) break;
       if ((s = p2p_barrier(ctx, stream)) != FERRUM_OK) break;
       launched(launch_rows_gather(log_n, inv, blocks, out, tw, b, scale, lb, stream),

@@ -1,15 +1,15 @@
-// Persistent batched-row FFT kernel with TMA bulk prefetch (sm_100a).
+// Bulk-copy (TMA) helpers and the persistent prefetching rows kernel
+// (sm_100a).
 //
-// Each CTA owns a strided sequence of tiles (FPB contiguous transforms =
-// 32 KiB for every N <= 4096). One elected thread moves the next tile from
-// HBM into a shared-memory staging buffer with a single
-// `cp.async.bulk.shared::cluster.global` copy that completes on an mbarrier,
-// so the HBM read of tile i+1 overlaps the register/shared-memory Stockham
-// stages of tile i and no load instruction of the computing warps waits on
-// DRAM latency. Results leave registers with streaming stores as in
-// fft_rows_kernel. Every mbarrier wait is bounded (%globaltimer, 1 s): on
-// expiry the CTA raises a device error flag that the host reads, waits
-// (again bounded) for its own copy in flight, and returns.
+// fft_rows_pf_kernel: each CTA owns a strided sequence of tiles (FPB
+// contiguous transforms). Once the last exchange of tile i has been read, one
+// elected thread moves tile i+1 from HBM into the CTA's exchange buffer with
+// a single `cp.async.bulk.shared::cluster.global` copy (no multicast; the
+// source is this GPU's own memory) that completes on an mbarrier, so the HBM
+// read overlaps the last stage and the stores of tile i. Every mbarrier wait
+// is bounded (%globaltimer, 1 s): on expiry the CTA raises a device error
+// flag that the host reads, waits (again bounded) for its own copy in flight,
+// and returns.
 #pragma once
 
 #include <stdint.h>
@@ -72,97 +72,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
           smem_u32(dst_smem)),
       "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
-}
-
-template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT>
-struct RowsTmaCfg {
-  using G = Geom<LOGN, LOGP>;
-  static constexpr int THREADS = FPB * G::T;
-  static constexpr int GROUPS_PER_HALFWARP = (G::T >= 16) ? 1 : (16 / G::T);
-  static constexpr int RS = RegionStride<LOGN, LOGP, GROUPS_PER_HALFWARP>::value;
-  static constexpr bool NEEDS_XCHG = G::STAGES > 1;
-  static constexpr size_t TILE_ELEMS = (size_t)FPB * G::N;
-  static constexpr size_t TILE_BYTES = TILE_ELEMS * sizeof(float2);
-  static constexpr size_t XCHG_BYTES = NEEDS_XCHG ? (size_t)FPB * RS * sizeof(float2) : 0;
-  // [staging tile][exchange regions][mbarrier]
-  static constexpr size_t SMEM_BYTES = TILE_BYTES + XCHG_BYTES + 16;
-  static constexpr int MIN_BLOCKS = 3;
-};
-
-template <int LOGN, int LOGP, int FPB, bool CONJ_IN, bool CONJ_OUT>
-__global__ void __launch_bounds__(RowsTmaCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::THREADS,
-                                  RowsTmaCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>::MIN_BLOCKS)
-fft_rows_tma_kernel(const float2* __restrict__ in, float2* out, const float2* __restrict__ tw,
-                    int64_t nfft, float scale, int* err) {
-  using G = Geom<LOGN, LOGP>;
-  using C = RowsTmaCfg<LOGN, LOGP, FPB, CONJ_IN, CONJ_OUT>;
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  float2* stage_buf = reinterpret_cast<float2*>(smem_raw);
-  float2* xchg = reinterpret_cast<float2*>(smem_raw + C::TILE_BYTES);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + C::TILE_BYTES + C::XCHG_BYTES);
-
-  const int g = threadIdx.x / G::T;
-  const int t = threadIdx.x % G::T;
-  const int64_t ntiles = (nfft + FPB - 1) / FPB;
-  float2* sm = xchg + (C::NEEDS_XCHG ? g * C::RS : 0);
-
-  auto tile_bytes = [&](int64_t tile) -> uint32_t {
-    const int64_t rows = (nfft - tile * FPB) < FPB ? (nfft - tile * FPB) : FPB;
-    return (uint32_t)(rows * G::N * sizeof(float2));
-  };
-
-  int64_t tile = blockIdx.x;
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && tile < ntiles) {
-    const uint32_t b = tile_bytes(tile);
-    mbar_arrive_expect_tx(bar, b);
-    bulk_g2s(stage_buf, in + tile * C::TILE_ELEMS, b, bar);
-  }
-
-  uint32_t phase = 0;
-  for (; tile < ntiles; tile += gridDim.x) {
-    const bool ok = mbar_wait_bounded(bar, phase);
-    if (__syncthreads_or(!ok)) {
-      // A copy did not land in time: report, give the copy one more bounded
-      // wait so no transfer targets this CTA's shared memory after exit.
-      if (threadIdx.x == 0) {
-        atomicOr(err, kErrWaitTimeout);
-        mbar_wait_bounded(bar, phase);
-      }
-      return;
-    }
-    phase ^= 1u;
-    const int64_t f = tile * FPB + g;
-    const bool valid = f < nfft;
-    float2 v[G::P];
-    const float2* src = stage_buf + g * G::N + t;
-#pragma unroll
-    for (int m = 0; m < G::P; ++m) v[m] = conj_if(src[G::T * m], CONJ_IN);
-    // Every thread has its values: order these generic-proxy reads before the
-    // async-proxy (TMA) write that refills the buffer, then let the refill go;
-    // the barrier also closes every exchange read of the previous tile.
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    const int64_t next = tile + gridDim.x;
-    if (threadIdx.x == 0 && next < ntiles) {
-      const uint32_t b = tile_bytes(next);
-      mbar_arrive_expect_tx(bar, b);
-      bulk_g2s(stage_buf, in + next * C::TILE_ELEMS, b, bar);
-    }
-    if constexpr (G::T <= 32)
-      run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
-    else
-      run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncBlock{});
-    if (valid) {
-      float2* dst = out + f * G::N + t;
-#pragma unroll
-      for (int m = 0; m < G::P; ++m) st_stream(dst + G::T * m, epilogue<CONJ_OUT>(v[m], scale));
-    }
-  }
 }
 
 // ----------------------------------------------------------------------------

@@ -192,7 +192,7 @@ ferrum_status ferrum_fft_1d_c2c_pow2_host(ferrum_device* dev, const void* in_hos
   if (log_n < 2 || log_n > kMaxLogN)
     return set_error(FERRUM_ERR_INVALID_ARG,
                      "fft_1d_c2c_pow2: log_n must be in [2, 26], got " + std::to_string(log_n));
-  if (batch == 0) return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2: batch must be positive");
+  if (ferrum_status s = check_elements(log_n, batch, "fft_1d_c2c_pow2")) return s;
   if (direction != 1 && direction != -1)
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2: direction must be +1 or -1");
   if (in_host == nullptr || out_host == nullptr)
@@ -209,7 +209,7 @@ ferrum_status ferrum_fft_2d_c2c_pow2_host(ferrum_device* dev, const void* in_hos
   if (log_n < 2 || log_n > kMaxSinglePassLogN)
     return set_error(FERRUM_ERR_INVALID_ARG,
                      "fft_2d_c2c_pow2: log_n must be in [2, 14], got " + std::to_string(log_n));
-  if (batch == 0) return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2: batch must be positive");
+  if (ferrum_status s = check_elements(2 * log_n, batch, "fft_2d_c2c_pow2")) return s;
   if (direction != 1 && direction != -1)
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_2d_c2c_pow2: direction must be +1 or -1");
   if (in_host == nullptr || out_host == nullptr)

@@ -1,172 +1,18 @@
-// Template dispatch from runtime (log_n, direction flags) to the pass kernels.
+// Launchers of the fused column kernel, the transposed-row kernel, the
+// distributed-transform kernels and the split-layout / elementwise kernels.
 #include <atomic>
 
 #include "dist_kernels.cuh"
 #include "fft_kernels.cuh"
 #include "fft_launch.h"
-#include "fft_rows_tma.cuh"
+#include "launch_common.cuh"
 #include "layout_kernels.cuh"
 #include "passes.h"
 
 namespace ferrum {
 namespace {
 
-constexpr int kRowsThreads = 256;   // batched rows: 256 threads per CTA up to N = 4096
-// The persistent TMA-prefetch rows kernel (fft_rows_tma.cuh) measured slower
-// than fft_rows_kernel on B200 for every N in 32..4096 at 2 GiB (4.87 vs 5.36
-// TB/s at N = 4096): the staging copy adds a shared-memory write and read per
-// element and costs one resident CTA per SM, and the kernel is bound by the
-// L1/shared pipe and issue rate rather than by DRAM latency. It stays off.
-constexpr bool kRowsTmaEnabled = false;
-// Sizes that use fft_rows_pf_kernel (prefetch into the exchange buffer): the
-// sizes with 32 values per thread, where one or two CTAs fill an SM and the
-// load phase is otherwise exposed (per 2 GiB: N = 16384 0.99 -> 0.85 ms,
-// N = 8192 0.79 -> 0.73 ms); with 16 values per thread (N <= 4096, four or
-// more CTAs per SM) it measured slower.
-constexpr bool rows_pf_enabled(int log_n) { return log_n == 13 || log_n == 14; }
-constexpr int kColsThreads = 512;   // strided passes: up to 16 columns / rows per CTA
-
-constexpr int rows_fpb(int log_n) {
-  return (plan_log_p(log_n) == log_n || (1 << (log_n - plan_log_p(log_n))) <= kRowsThreads)
-             ? kRowsThreads / (1 << (log_n - plan_log_p(log_n)))
-             : 1;
-}
-constexpr int cols_fpb(int log_n, int threads = kColsThreads) {
-  // clamp(threads / T, 1, 16)
-  return (threads >> (log_n - plan_log_p(log_n))) < 1
-             ? 1
-             : ((threads >> (log_n - plan_log_p(log_n))) > 16
-                    ? 16
-                    : (threads >> (log_n - plan_log_p(log_n))));
-}
-// The SFU-twiddle column passes of the multi-pass 1D transform are latency-
-// bound (their block barriers keep a CTA's warps in step); 256-thread CTAs,
-// more of them per SM and out of step, measured 2-3 % faster at 2^18 and 2^19
-// and level elsewhere, although N1 = 1024 then reads 32-byte row segments.
-constexpr int kSfuColsThreads = 256;
-
-// Raise the dynamic shared-memory limit once per (kernel, device). `done` is
-// a per-instantiation flag word owned by the caller (one bit per device).
-template <class K>
-cudaError_t ensure_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done) {
-  if (bytes <= 48 * 1024) return cudaSuccess;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
-  return e;
-}
-
-int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
-
-// Every launch below is followed by cudaGetLastError(), which reports the
-// last error of any runtime call in the process. Consuming an earlier,
-// unrelated error (a failed lookup or allocation by the caller) first keeps it
-// from being reported as a failure of this launch; sticky errors persist
-// and are still reported.
-inline void clear_stale_error() { (void)cudaGetLastError(); }
-
-template <int LOGN, bool CI, bool CO>
-cudaError_t rows_impl(const float2* in, float2* out, const float2* tw, int64_t nfft, float scale,
-                      int log_block, int64_t block_rows, cudaStream_t s) {
-  constexpr int LOGP = plan_log_p(LOGN);
-  constexpr int FPB = rows_fpb(LOGN);
-  using C = RowsCfg<LOGN, LOGP, FPB, CI, CO>;
-  auto k = fft_rows_kernel<LOGN, LOGP, FPB, CI, CO>;
-  static std::atomic<uint64_t> smem_done{0};
-  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
-  if (e != cudaSuccess) return e;
-  const int64_t blocks = ceil_div(nfft, FPB);
-  clear_stale_error();
-  k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, log_block,
-                                                        block_rows);
-  return cudaGetLastError();
-}
-
-// Persistent TMA-prefetch variant (fft_rows_tma.cuh): one CTA per resident
-// slot, every CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
-template <int LOGN, bool CI, bool CO>
-cudaError_t rows_tma_impl(const float2* in, float2* out, const float2* tw, int64_t nfft,
-                          float scale, int* err, cudaStream_t s) {
-  constexpr int LOGP = plan_log_p(LOGN);
-  constexpr int FPB = rows_fpb(LOGN);
-  using C = RowsTmaCfg<LOGN, LOGP, FPB, CI, CO>;
-  auto k = fft_rows_tma_kernel<LOGN, LOGP, FPB, CI, CO>;
-  static std::atomic<uint64_t> smem_done{0};
-  static std::atomic<int> grid_cache[64];
-  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
-  if (e != cudaSuccess) return e;
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  int resident = grid_cache[dev & 63].load(std::memory_order_relaxed);
-  if (resident == 0) {
-    int per_sm = 0, sms = 0;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, C::THREADS, C::SMEM_BYTES)) !=
-        cudaSuccess)
-      return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-      return e;
-    resident = (per_sm < 1 ? 1 : per_sm) * sms;
-    grid_cache[dev & 63].store(resident, std::memory_order_relaxed);
-  }
-  const int64_t tiles = ceil_div(nfft, FPB);
-  const int64_t grid = tiles < resident ? tiles : resident;
-  clear_stale_error();
-  k<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, err);
-  return cudaGetLastError();
-}
-
-// Persistent rows kernel prefetching into its own exchange buffer
-// (fft_rows_tma.cuh, fft_rows_pf_kernel).
-template <int LOGN, bool CI, bool CO>
-cudaError_t rows_pf_impl(const float2* in, float2* out, const float2* tw, int64_t nfft,
-                         float scale, int* err, cudaStream_t s) {
-  constexpr int LOGP = plan_log_p(LOGN);
-  constexpr int FPB = rows_fpb(LOGN);
-  using C = RowsPfCfg<LOGN, LOGP, FPB, CI, CO>;
-  auto k = fft_rows_pf_kernel<LOGN, LOGP, FPB, CI, CO>;
-  static std::atomic<uint64_t> smem_done{0};
-  static std::atomic<int> grid_cache[64];
-  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
-  if (e != cudaSuccess) return e;
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  int resident = grid_cache[dev & 63].load(std::memory_order_relaxed);
-  if (resident == 0) {
-    int per_sm = 0, sms = 0;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, C::THREADS, C::SMEM_BYTES)) !=
-        cudaSuccess)
-      return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-      return e;
-    resident = (per_sm < 1 ? 1 : per_sm) * sms;
-    grid_cache[dev & 63].store(resident, std::memory_order_relaxed);
-  }
-  const int64_t tiles = ceil_div(nfft, FPB);
-  const int64_t grid = tiles < resident ? tiles : resident;
-  clear_stale_error();
-  k<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, nfft, scale, err);
-  return cudaGetLastError();
-}
-
-template <int LOGN, bool CI, bool CO, int TW>
-cudaError_t pass_impl(const float2* in, float2* out, const float2* tw, const PassArgs& a,
-                      cudaStream_t s) {
-  constexpr int LOGP = plan_log_p(LOGN);
-  constexpr int FPB = cols_fpb(LOGN, TW == 2 ? kSfuColsThreads : kColsThreads);
-  using C = PassCfg<LOGN, LOGP, FPB, CI, CO, TW>;
-  auto k = fft_pass_kernel<LOGN, LOGP, FPB, CI, CO, TW>;
-  static std::atomic<uint64_t> smem_done{0};
-  cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
-  if (e != cudaSuccess) return e;
-  const int64_t blocks = ceil_div(a.nfft, FPB);
-  clear_stale_error();
-  k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);
-  return cudaGetLastError();
-}
+using namespace launch_detail;
 
 template <int L1, int L2, int W, int THREADS, int MINB, bool CI, bool CO>
 cudaError_t cols_l2_impl(const float2* in, float2* out, float2* ws, const float2* tw1,
@@ -210,54 +56,6 @@ cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const R
   clear_stale_error();
   k<<<(unsigned)blocks, C::THREADS, C::SMEM_BYTES, s>>>(in, out, tw, a);
   return cudaGetLastError();
-}
-
-template <int LOGN>
-cudaError_t rows_dispatch(bool ci, bool co, const float2* in, float2* out, const float2* tw,
-                          int64_t nfft, float scale, int lb, int64_t br, int* err, cudaStream_t s) {
-  if constexpr (rows_pf_enabled(LOGN)) {
-    if (err != nullptr && lb >= LOGN && ((uintptr_t)in & 15u) == 0) {
-      if (ci && co) return rows_pf_impl<LOGN, true, true>(in, out, tw, nfft, scale, err, s);
-      if (ci) return rows_pf_impl<LOGN, true, false>(in, out, tw, nfft, scale, err, s);
-      if (co) return rows_pf_impl<LOGN, false, true>(in, out, tw, nfft, scale, err, s);
-      return rows_pf_impl<LOGN, false, false>(in, out, tw, nfft, scale, err, s);
-    }
-  }
-  if constexpr (kRowsTmaEnabled && LOGN >= 4 && LOGN <= 12) {
-    // TMA bulk copies need a 16-byte aligned source; blocked stores keep the
-    // plain kernel.
-    if (err != nullptr && lb >= LOGN && ((uintptr_t)in & 15u) == 0) {
-      if (ci && co) return rows_tma_impl<LOGN, true, true>(in, out, tw, nfft, scale, err, s);
-      if (ci) return rows_tma_impl<LOGN, true, false>(in, out, tw, nfft, scale, err, s);
-      if (co) return rows_tma_impl<LOGN, false, true>(in, out, tw, nfft, scale, err, s);
-      return rows_tma_impl<LOGN, false, false>(in, out, tw, nfft, scale, err, s);
-    }
-  }
-  if (ci && co) return rows_impl<LOGN, true, true>(in, out, tw, nfft, scale, lb, br, s);
-  if (ci) return rows_impl<LOGN, true, false>(in, out, tw, nfft, scale, lb, br, s);
-  if (co) return rows_impl<LOGN, false, true>(in, out, tw, nfft, scale, lb, br, s);
-  return rows_impl<LOGN, false, false>(in, out, tw, nfft, scale, lb, br, s);
-}
-
-// Instantiates exactly the combinations pass_flags_supported() allows.
-template <int LOGN>
-cudaError_t pass_dispatch(bool ci, bool co, bool tw, const float2* in, float2* out,
-                          const float2* stw, const PassArgs& a, cudaStream_t s) {
-  if (!pass_flags_supported(ci, co, tw)) return cudaErrorInvalidValue;
-  if (tw && a.tw_sfu) {
-    if constexpr (pass_sfu_supported(LOGN)) {
-      if (ci) return pass_impl<LOGN, true, false, 2>(in, out, stw, a, s);
-      return pass_impl<LOGN, false, false, 2>(in, out, stw, a, s);
-    }
-    return cudaErrorInvalidValue;
-  }
-  if (tw) {
-    if (ci) return pass_impl<LOGN, true, false, 1>(in, out, stw, a, s);
-    return pass_impl<LOGN, false, false, 1>(in, out, stw, a, s);
-  }
-  if (ci) return pass_impl<LOGN, true, false, 0>(in, out, stw, a, s);
-  if (co) return pass_impl<LOGN, false, true, 0>(in, out, stw, a, s);
-  return pass_impl<LOGN, false, false, 0>(in, out, stw, a, s);
 }
 
 template <int LOGN>
@@ -357,8 +155,6 @@ cudaError_t launch_block_gather(const float2* in, float2* out, int64_t nblocks, 
   return cudaGetLastError();
 }
 
-#define FERRUM_CASE_4_14(X) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
-
 cudaError_t launch_rows_scatter(int log_n, bool conj_in, const float2* in, const PeerPtrs& dst,
                                 const float2* tw, int64_t nfft, int log_b, cudaStream_t stream) {
   if (log_b < 1 || log_b > log_n) return cudaErrorInvalidValue;
@@ -448,26 +244,6 @@ cudaError_t launch_interleave(const float* re, const float* im, float2* out, int
   return cudaGetLastError();
 }
 
-#define FERRUM_CASE_2_14(X) \
-  X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
-
-cudaError_t launch_rows(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
-                        const float2* tw, int64_t nfft, float scale, cudaStream_t stream,
-                        int log_block, int* err_flag, int64_t block_rows) {
-  if (log_block < 0 || log_block > log_n) log_block = log_n;
-  if (block_rows <= 0) block_rows = nfft;
-  switch (log_n) {
-#define X(L) \
-  case L:    \
-    return rows_dispatch<L>(conj_in, conj_out, in, out, tw, nfft, scale, log_block, block_rows, \
-                            err_flag, stream);
-    FERRUM_CASE_2_14(X)
-#undef X
-    default:
-      return cudaErrorInvalidValue;
-  }
-}
-
 cudaError_t launch_rows_split(int log_n, bool conj_in, bool conj_out, const float* in_re,
                               const float* in_im, float* out_re, float* out_im, const float2* tw,
                               int64_t nfft, float scale, cudaStream_t stream) {
@@ -481,20 +257,6 @@ cudaError_t launch_rows_split(int log_n, bool conj_in, bool conj_out, const floa
     if (conj_out)                                                                             \
       return rows_split_impl<L, false, true>(in_re, in_im, out_re, out_im, tw, nfft, scale, stream); \
     return rows_split_impl<L, false, false>(in_re, in_im, out_re, out_im, tw, nfft, scale, stream);
-    FERRUM_CASE_2_14(X)
-#undef X
-    default:
-      return cudaErrorInvalidValue;
-  }
-}
-
-cudaError_t launch_pass(int log_n, bool conj_in, bool conj_out, bool tw, const float2* in,
-                        float2* out, const float2* stage_tw, const PassArgs& args,
-                        cudaStream_t stream) {
-  switch (log_n) {
-#define X(L) \
-  case L:    \
-    return pass_dispatch<L>(conj_in, conj_out, tw, in, out, stage_tw, args, stream);
     FERRUM_CASE_2_14(X)
 #undef X
     default:

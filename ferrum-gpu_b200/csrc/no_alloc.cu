@@ -1,7 +1,8 @@
 // Allocation-free 1D entry point: ferrum_fft_1d_c2c_pow2_noalloc.
 //
-// Lengths above 2^14 run the two-pass four-step transform, whose first pass
-// writes an N*batch intermediate. ferrum_fft_1d_c2c_pow2 takes that scratch
+// Lengths above 2^14 run the multi-pass transform (two passes up to 2^21,
+// three from 2^22), whose passes keep an N*batch intermediate in scratch
+// memory. ferrum_fft_1d_c2c_pow2 takes that scratch
 // from a stream-ordered pool and ferrum_fft_1d_c2c_pow2_ws from the caller;
 // this entry point instead uses one file-scope __device__ array, so the call
 // itself never allocates device memory. It exists for callers that cannot
@@ -17,15 +18,17 @@
 // run the same single-pass kernel as ferrum_fft_1d_c2c_pow2.
 //
 // The array is shared by every call on a device and keeps the last call's
-// contents. Nothing in it needs to start at zero: pass A writes every
-// scratch element that pass B later reads. Calls whose kernels overlap on the
+// contents. Nothing in it needs to start at zero: every pass reads only
+// scratch elements that an earlier pass of the same call wrote. Calls whose kernels overlap on the
 // GPU (different streams, no ordering between them) race on the array.
 //
 // The host-side name of a __device__ array is not a device address, so the
 // first call on each device looks the address up with cudaGetSymbolAddress
-// while that device is current, and caches it. That set-up happens inside
-// the first call, so the first call on a device should come before any
-// stream capture.
+// while that device is current, and caches it; a failed lookup is not
+// cached, so a later call tries again. That set-up happens inside the first
+// call, so the first call on a device should come before any stream capture.
+// cudaDeviceReset destroys the module's device copy: a process that resets a
+// device must not call this entry point on it again.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -42,26 +45,24 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float2 g_noalloc_scratch[kNoAllocScratchElems];
 
-struct ScratchAddress {
-  std::once_flag once;
-  float2* ptr = nullptr;
-  cudaError_t status = cudaSuccess;
-};
-ScratchAddress g_scratch_address[kMaxDevices];
+std::mutex g_scratch_mu;
+float2* g_scratch_address[kMaxDevices] = {};  // guarded by g_scratch_mu; NULL until looked up
 
 // Device address of the scratch on `ordinal`, which must be the current device.
 ferrum_status scratch_address(int ordinal, float2** out) {
   if (ordinal < 0 || ordinal >= kMaxDevices)
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2_noalloc: device ordinal " +
                                                  std::to_string(ordinal) + " out of range");
-  ScratchAddress& a = g_scratch_address[ordinal];
-  std::call_once(a.once, [&a] {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_address[ordinal] == nullptr) {
     void* p = nullptr;
-    a.status = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    a.ptr = static_cast<float2*>(p);
-  });
-  if (a.status != cudaSuccess) return cuda_error(a.status, "cudaGetSymbolAddress(no-alloc scratch)");
-  *out = a.ptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                        "cudaGetSymbolAddress(no-alloc scratch)");
+    g_scratch_address[ordinal] = static_cast<float2*>(p);
+  }
+  *out = g_scratch_address[ordinal];
   return FERRUM_OK;
 }
 
@@ -80,8 +81,7 @@ extern "C" ferrum_status ferrum_fft_1d_c2c_pow2_noalloc(ferrum_device* dev, cons
   if (log_n < 2 || log_n > kMaxLogN)
     return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2_noalloc: log_n must be in [2, 26], got " +
                                                  std::to_string(log_n));
-  if (batch == 0)
-    return set_error(FERRUM_ERR_INVALID_ARG, "fft_1d_c2c_pow2_noalloc: batch must be positive");
+  if (ferrum_status s = check_elements(log_n, batch, "fft_1d_c2c_pow2_noalloc")) return s;
   if (direction != 1 && direction != -1)
     return set_error(FERRUM_ERR_INVALID_ARG,
                      "fft_1d_c2c_pow2_noalloc: direction must be +1 (forward) or -1 (inverse), got " +

@@ -75,4 +75,13 @@ ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* i
 // Reads and clears the device error flag; FERRUM_ERR_TIMEOUT if it was set.
 ferrum_status check_device_flag(ferrum_device* dev);
 
+// Largest number of complex values one call may cover: 2^36 (512 GiB, more
+// than a B200 holds). Below it every byte count, element index and grid size
+// the plans form stays far from overflow.
+constexpr int kMaxLogElems = 36;
+// FERRUM_ERR_INVALID_ARG unless batch * 2^elem_log <= 2^kMaxLogElems
+// (elem_log = log_n for 1D, 2 * log_n for 2D); checked before any size is
+// computed from the batch.
+ferrum_status check_elements(int elem_log, size_t batch, const char* what);
+
 }  // namespace ferrum

@@ -70,11 +70,22 @@ def test_workspace_and_launch_counts(capi):
 
 
 @pytest.mark.parametrize("log_n,batch,kind", [(1, 1, 1), (27, 1, 1), (10, 0, 1), (15, 1, 2),
-                                              (10, 1, 3)])
+                                              (10, 1, 3),
+                                              # N * batch above 2^36 complex values: rejected
+                                              # before any size is formed (2^44 + 1 would wrap
+                                              # the byte count at 2^20)
+                                              (20, (1 << 44) + 1, 1), (20, (1 << 16) + 1, 1),
+                                              (14, (1 << 8) + 1, 2), (2, (1 << 34) + 1, 1)])
 def test_invalid_sizes_rejected(capi, log_n, batch, kind):
     with pytest.raises(capi.FerrumError) as e:
         capi.workspace_bytes(log_n, batch, kind)
     assert e.value.status == capi.FERRUM_ERR_INVALID_ARG
+
+
+def test_largest_allowed_batch_sizes(capi):
+    # exactly 2^36 complex values per call is still accepted
+    assert capi.workspace_bytes(20, 1 << 16, 1) == (1 << 36) * 8
+    assert capi.workspace_bytes(2, 1 << 34, 1) == 0
 
 
 def test_null_device_rejected(capi):

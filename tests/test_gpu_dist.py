@@ -132,6 +132,103 @@ def test_distributed_2d_matches_oracle(world, p2p):
             assert rt < 1e-4, (rank, log_n, rt)
 
 
+def _sampled_rows(n, world, per_rank=2):
+    """Output rows checked at 16384^2: `per_rank` rows inside every rank's row slab."""
+    b = n // world
+    rows = []
+    for q in range(world):
+        rows += [q * b + (37 * q + 5) % b, q * b + b - 1 - (11 * q) % b][:per_rank]
+    return np.array(sorted(set(rows)))
+
+
+def _worker_16384(rank, world, port, p2p, q):
+    """16384^2 on `world` ranks. Each rank makes only its own row slab (seeded
+    per rank). The reference for a sample of output rows k is built without
+    any rank holding the whole image: each rank forms the column DFT of its
+    slab at the sampled frequencies in float64, sum_n1 W_N^(k n1) x[n1, :]
+    over its rows, the partial sums are added over the ranks (gloo), and the
+    oracle's 1D FFT of each summed row gives output row k of the 2D
+    transform (rows first or columns first give the same result)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    for p in (REPO, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["FERRUM_DIST_P2P"] = "1" if p2p else "0"
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=300))
+        torch.cuda.set_device(rank)
+        import oracle
+        from ferrum_gpu import capi
+        from ferrum_gpu import dist as fdist
+
+        log_n = 14
+        n = 1 << log_n
+        r0, rows = fdist.slab_bounds(n, world, rank)
+        rng = np.random.default_rng([log_n, rank])
+        slab_h = (rng.standard_normal((rows, n), dtype=np.float32)
+                  + 1j * rng.standard_normal((rows, n), dtype=np.float32)).astype(np.complex64)
+        ks = _sampled_rows(n, world)
+        n1 = np.arange(r0, r0 + rows, dtype=np.float64)
+        w = np.exp(-2j * np.pi * np.outer(ks, n1) / n)          # (|S|, rows)
+        part = torch.from_numpy(w @ slab_h.astype(np.complex128))  # (|S|, n)
+        part = torch.view_as_real(part).contiguous()
+        dist.all_reduce(part)
+        colsum = torch.view_as_complex(part).numpy().astype(np.complex64)
+        ref = oracle.fft_1d(colsum.reshape(-1), log_n, threads=2).reshape(len(ks), n)
+
+        dev = capi.DeviceHandle(rank)
+        ctx = fdist.Dist2D(dev, timeout_ms=60000)
+        slab = torch.from_numpy(slab_h).cuda()
+        errs = []
+        out = ctx.fft_2d_tensor(slab, log_n, "forward", False)            # rows -> rows
+        mine = [i for i, k in enumerate(ks) if r0 <= k < r0 + rows]
+        got = out.cpu().numpy()
+        for i in mine:
+            errs.append(float(np.max(np.abs(got[ks[i] - r0] - ref[i])) / np.max(np.abs(ref[i]))))
+        cols = ctx.fft_2d_tensor(slab, log_n, "forward", False, out_layout="cols")  # rows -> cols
+        got_c = cols.cpu().numpy()                                        # (n, rows)
+        for i, k in enumerate(ks):
+            seg = ref[i, r0:r0 + rows]
+            errs.append(float(np.max(np.abs(got_c[k] - seg)) / np.max(np.abs(ref[i]))))
+        back = ctx.fft_2d_tensor(cols, log_n, "inverse", True, in_layout="cols")
+        rt = float((back - slab).abs().max() / slab.abs().max())
+        back_r = ctx.fft_2d_tensor(out, log_n, "inverse", True)
+        rt = max(rt, float((back_r - slab).abs().max() / slab.abs().max()))
+        path = ctx.peer_path
+        ctx.close()
+        dev.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok", (path, len(mine), max(errs), rt)))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("p2p", [True, False], ids=["peer", "nccl"])
+def test_distributed_2d_16384_sampled(world, p2p):
+    """BASELINE config 5 at its full size: sampled output rows (every rank's
+    row slab holds some) of the 16384^2 transform against the oracle, both
+    output layouts, and the round trips."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = _spawn(_worker_16384, world, p2p, wait_s=900)
+    for rank, status, payload in out:
+        assert status == "ok", f"rank {rank}: {payload}"
+        path, n_mine, err, rt = payload
+        assert path == (1 if p2p else 0), (rank, path)
+        assert n_mine >= 1, rank
+        assert err < 1e-4, (rank, err)
+        assert rt < 1e-4, (rank, rt)
+
+
 def _barrier_worker(rank, world, port, q):
     import datetime
     import faulthandler

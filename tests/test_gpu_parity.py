@@ -12,6 +12,8 @@ Parseval, plus oracle parity on a sample of rows.
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 
@@ -19,6 +21,7 @@ from conftest import gpu_available, max_rel_err, rand_c64
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-4
+THREADS = max(1, min(32, os.cpu_count() or 1))  # oracle lanes in parallel
 
 torch = pytest.importorskip("torch")
 if not torch.cuda.is_available():
@@ -212,9 +215,11 @@ def test_2d_in_place(capi, dev, oracle_mod, log_n, batch, direction, normalize):
     assert max_rel_err(got, ref) < TOL
 
 
-def test_2d_16384_properties(capi, dev, oracle_mod):
-    """16384 x 16384 (the distributed config, here on one GPU): row 0 of the result is
-    the 1D FFT of the column sums; round trip recovers the input."""
+def test_2d_16384_full_image(capi, dev, oracle_mod):
+    """16384 x 16384 (the distributed config, here on one GPU, standard normal
+    inputs): the whole forward image against the oracle's 2D (row pass,
+    transpose, row pass, transpose), then the inverse with 1/N^2 against the
+    oracle's inverse of the same spectrum, and the round trip."""
     log_n = 14
     n = 1 << log_n
     g = torch.Generator(device="cuda").manual_seed(14)
@@ -224,11 +229,17 @@ def test_2d_16384_properties(capi, dev, oracle_mod):
     s = _stream()
     capi.fft_2d(dev, x.data_ptr(), y.data_ptr(), log_n, 1, "forward", False, s)
     torch.cuda.synchronize()
-    colsum = x.to(torch.complex128).sum(dim=0).to(torch.complex64).cpu().numpy()
-    ref = oracle_mod.fft_1d(colsum, log_n)
-    assert max_rel_err(y[0].cpu().numpy(), ref) < TOL
-    capi.fft_2d(dev, y.data_ptr(), y.data_ptr(), log_n, 1, "inverse", True, s)
+    xh = x.cpu().numpy()
+    ref = oracle_mod.fft_2d(xh, log_n, "forward", False, threads=THREADS)
+    assert max_rel_err(y.cpu().numpy(), ref) < TOL
+    # the inverse from the oracle's own spectrum, so both see the same input
+    yr = torch.from_numpy(ref).to("cuda")
+    capi.fft_2d(dev, yr.data_ptr(), y.data_ptr(), log_n, 1, "inverse", True, s)
     torch.cuda.synchronize()
+    ref_inv = oracle_mod.fft_2d(ref, log_n, "inverse", True, threads=THREADS)
+    del ref
+    assert max_rel_err(y.cpu().numpy(), ref_inv) < TOL
+    assert max_rel_err(ref_inv, xh) < TOL
     assert float((y - x).abs().max() / x.abs().max()) < TOL
 
 
@@ -275,9 +286,12 @@ def test_config_sizes_properties(capi, dev, oracle_mod, log_n, batch):
     s = _stream()
     capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), log_n, batch, "forward", False, s)
     torch.cuda.synchronize()
-    rows = torch.tensor([0, 1, batch // 2, batch - 1], device="cuda")
-    ref = oracle_mod.fft_1d(x[rows].cpu().numpy().reshape(-1), log_n)
-    assert max_rel_err(y[rows].cpu().numpy(), ref) < TOL
+    # 64 rows spread over the batch (the first, the last and 62 between,
+    # seeded) against the oracle
+    pick = np.random.default_rng(100 + log_n).choice(np.arange(1, batch - 1), 62, replace=False)
+    rows = torch.tensor(np.r_[0, np.sort(pick), batch - 1], device="cuda")
+    ref = oracle_mod.fft_1d(x[rows].cpu().numpy().reshape(-1), log_n, threads=THREADS)
+    assert max_rel_err(y[rows].cpu().numpy().reshape(-1), ref) < TOL
     # Parseval: sum |X|^2 = N sum |x|^2 (per row, in float64)
     ex = (x.abs().double() ** 2).sum(dim=1) * n
     ey = (y.abs().double() ** 2).sum(dim=1)
@@ -299,8 +313,8 @@ def test_config_sizes_properties(capi, dev, oracle_mod, log_n, batch):
 
 @pytest.mark.parametrize("log_n,batch", [(20, 64), (24, 4)])
 def test_large_n_config_properties(capi, dev, oracle_mod, log_n, batch):
-    """Large-N sizes 2^20 x 64 and 2^24 x 4 (standard normal inputs): one transform against the
-    oracle, the full batch through a round trip."""
+    """Large-N sizes 2^20 x 64 and 2^24 x 4 (standard normal inputs): every transform
+    against the oracle, forward and inverse (1/N), and the full batch through a round trip."""
     n = 1 << log_n
     g = torch.Generator(device="cuda").manual_seed(log_n)
     x = torch.complex(torch.randn(batch, n, device="cuda", generator=g),
@@ -309,8 +323,20 @@ def test_large_n_config_properties(capi, dev, oracle_mod, log_n, batch):
     s = _stream()
     capi.fft_1d(dev, x.data_ptr(), y.data_ptr(), log_n, batch, "forward", False, s)
     torch.cuda.synchronize()
-    ref = oracle_mod.fft_1d(x[batch - 1].cpu().numpy(), log_n, threads=8)
-    assert max_rel_err(y[batch - 1].cpu().numpy(), ref) < TOL
+    xh = x.cpu().numpy()
+    ref = oracle_mod.fft_1d(xh.reshape(-1), log_n, threads=THREADS).reshape(batch, n)
+    yh = y.cpu().numpy()
+    for i in range(batch):
+        assert max_rel_err(yh[i], ref[i]) < TOL, i
+    yr = torch.from_numpy(ref).to("cuda")
+    z = torch.empty_like(yr)
+    capi.fft_1d(dev, yr.data_ptr(), z.data_ptr(), log_n, batch, "inverse", True, s)
+    torch.cuda.synchronize()
+    ref_inv = oracle_mod.fft_1d(ref.reshape(-1), log_n, "inverse", True,
+                                threads=THREADS).reshape(batch, n)
+    zh = z.cpu().numpy()
+    for i in range(batch):
+        assert max_rel_err(zh[i], ref_inv[i]) < TOL, i
     capi.fft_1d(dev, y.data_ptr(), y.data_ptr(), log_n, batch, "inverse", True, s)
     torch.cuda.synchronize()
     assert float((y - x).abs().max() / x.abs().max()) < TOL
