@@ -40,7 +40,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr", f"-I{INCLUDE}"] + ARCH
 
-CU_SOURCES = ["launch_rows.cu", "launch_pass.cu", "launch_misc.cu", "capi.cu", "host_path.cu", "dist.cu",
+CU_SOURCES = ["launch_rows.cu", "launch_pass.cu", "launch_misc.cu", "launch_tile.cu", "capi.cu", "host_path.cu", "dist.cu",
               "no_alloc.cu", "substrate.cu"]
 LIB = os.path.join(PKG, "libferrum_fft.so")
 EXT = os.path.join(PKG, "_native" + sysconfig.get_config_var("EXT_SUFFIX"))

@@ -132,11 +132,21 @@ ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* i
           a.tw_lo = tw4_lo_table(dev, a.log_m);
           a.tw_hi = tw4_hi_table(dev, a.log_m);
         }
-        e = launch_pass(d.log_n, d.conj_in, d.conj_out, a.log_m > 0, src, dst, stw, a, stream);
+        e = cudaErrorNotSupported;
+        if (d.tile != TileMode::None)
+          e = launch_pass_tile(d.tile, d.tile_w, d.log_n, d.conj_in, d.conj_out, a.log_m > 0, src,
+                               dst, stw, a, dev->err_flag, stream);
+        if (e == cudaErrorNotSupported)
+          e = launch_pass(d.log_n, d.conj_in, d.conj_out, a.log_m > 0, src, dst, stw, a, stream);
         break;
       }
       case PassKind::RowsT:
-        e = launch_rows_t(d.log_n, d.conj_out, src, dst, stw, d.ra, stream);
+        e = cudaErrorNotSupported;
+        if (d.tile != TileMode::None)
+          e = launch_rows_t_tile(d.tile, d.tile_w, d.log_n, d.conj_out, src, dst, stw, d.ra,
+                                 stream);
+        if (e == cudaErrorNotSupported)
+          e = launch_rows_t(d.log_n, d.conj_out, src, dst, stw, d.ra, stream);
         break;
       case PassKind::ColsL2: {
         ColsL2Args a = d.ca;

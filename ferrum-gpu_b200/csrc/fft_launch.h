@@ -11,6 +11,7 @@ struct RowsTArgs;
 struct ColsL2Args;
 struct PeerPtrs;
 struct PeerFlags;
+enum class TileMode : int;
 
 // Batched contiguous transforms of length 2^log_n (2 <= log_n <= 14). With
 // 0 <= log_block < log_n the output is stored blocked: element e of row f at
@@ -48,9 +49,23 @@ cudaError_t launch_cols_l2(int log_n, bool conj_in, bool conj_out, const float2*
                            float2* ws, const float2* tw1, const float2* tw2, const ColsL2Args& args,
                            cudaStream_t stream);
 
+// The same strided pass in a persistent tile kernel (launch_tile.cu) of the
+// given family and tile width; cudaErrorNotSupported when that kernel is not
+// compiled for these arguments or the layout does not meet its conditions
+// (the caller then runs launch_pass). `err` is the device flag of the TMA
+// kernel's bounded waits.
+cudaError_t launch_pass_tile(TileMode mode, int w, int log_n, bool conj_in, bool conj_out,
+                             bool tw, const float2* in, float2* out, const float2* stage_tw,
+                             const PassArgs& args, int* err, cudaStream_t stream);
+
 // Rows of length 2^log_n (4 <= log_n <= 14) stored transposed.
 cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* out,
                           const float2* tw, const RowsTArgs& args, cudaStream_t stream);
+// The same in a persistent tile kernel; cudaErrorNotSupported as for
+// launch_pass_tile (the caller then runs launch_rows_t).
+cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_n, bool conj_out, const float2* in,
+                               float2* out, const float2* tw, const RowsTArgs& args,
+                               cudaStream_t stream);
 
 // Distributed 2D over peer memory (dist_kernels.cuh); 4 <= log_n <= 14,
 // B = 2^log_b columns per rank. Row FFTs of `nfft` local rows whose output

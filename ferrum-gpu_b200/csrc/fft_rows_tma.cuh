@@ -15,64 +15,9 @@
 #include <stdint.h>
 
 #include "fft_kernels.cuh"
+#include "tma_util.cuh"
 
 namespace ferrum {
-
-constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait
-constexpr int kErrWaitTimeout = 1;
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(phase)
-      : "memory");
-  return done != 0;
-}
-
-// Bounded wait for `phase` of `bar`; false after kWaitTimeoutNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
-  if (mbar_try_wait(bar, phase)) return true;
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, phase)) {
-    if (global_ns() - t0 > kWaitTimeoutNs) return false;
-  }
-  return true;
-}
-
-// Global -> shared bulk copy of `bytes` (multiple of 16, both addresses
-// 16-byte aligned) completing on `bar`.
-__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
-                                         uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst_smem)),
-      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // ----------------------------------------------------------------------------
 // Persistent rows kernel that prefetches into the exchange buffer itself.

@@ -5,10 +5,11 @@
 // Every pass reads and writes each element once, with row segments of at
 // least 64-128 bytes:
 //   * 1D, N <= 2^14: one fft_rows_kernel pass.
-//   * 1D, 2^15..2^21: two passes, N = N1*N2, x[n2 + N2*n1]:
+//   * 1D, 2^15..2^23: two passes, N = N1*N2, x[n2 + N2*n1]:
 //       A  DFT over n1 (columns of the N1 x N2 view), times W_N^(n2*k1);
 //       B  DFT over n2 (rows), stored transposed to X[k1 + N1*k2].
-//   * 1D, 2^22..2^26: three passes, N = N1*N2*N3, x[n3 + N3*n2 + N3*N2*n1]:
+//     (2^19..2^23 run both passes in the persistent tile kernels).
+//   * 1D, 2^24..2^26: three passes, N = N1*N2*N3, x[n3 + N3*n2 + N3*N2*n1]:
 //       1  DFT over n1, times W_{N1 N2}^(n2*k1);
 //       2  DFT over n2, times W_N^(n3*(k1 + N1*k2));
 //       3  DFT over n3 (rows), stored to X[k1 + N1*k2 + N1*N2*k3].
@@ -34,9 +35,22 @@ namespace ferrum {
 enum class PassKind : int { Rows = 0, Pass = 1, RowsT = 2, ColsL2 = 3 };
 enum class PassBuf : int { In = 0, Out = 1, Ws = 2 };
 
+// Kernel family of a Pass / RowsT pass. The tile kernels (fft_tile_kernels.cuh)
+// compute exactly what the plain kernels do over the same PassArgs /
+// RowsTArgs, in persistent CTAs that each take tiles of `tile_w` adjacent
+// transforms. They need 16-byte aligned buffers (the runtime falls back to the
+// plain kernel otherwise).
+enum class TileMode : int {
+  None = 0,     // fft_pass_kernel / fft_rows_t_kernel
+  Prefetch = 1, // fft_cols_tile_kernel (tensor-map L2 prefetch) / fft_rows_t_tile_kernel
+  Tma = 2,      // fft_cols_tma_kernel (TMA tile load and store) / fft_rows_t_tma_kernel (TMA store)
+};
+
 struct PassDesc {
   PassKind kind;
   int log_n;  // transform length of the pass
+  TileMode tile = TileMode::None;
+  int tile_w = 0;
   bool conj_in, conj_out;
   PassBuf src, dst;
   // Rows
@@ -67,8 +81,8 @@ constexpr bool pass_flags_supported(bool ci, bool co, bool tw) {
 }
 
 // Pass lengths compiled with SFU twiddle factors (the column passes of the
-// multi-pass 1D transform, 2^15..2^26, have lengths 2^7..2^10).
-constexpr bool pass_sfu_supported(int log_n) { return log_n >= 7 && log_n <= 10; }
+// multi-pass 1D transform, 2^15..2^26, have lengths 2^7..2^11).
+constexpr bool pass_sfu_supported(int log_n) { return log_n >= 7 && log_n <= 11; }
 
 inline PassDesc make_rows(int log_n, int64_t nfft, bool ci, bool co, float scale, PassBuf src,
                           PassBuf dst, int log_block = -1, int64_t block_rows = 0) {
@@ -170,7 +184,37 @@ inline int64_t cols_l2_ws_elems(int log_n) {
 }
 
 // Passes of a multi-pass 1D transform.
-inline int plan_1d_passes(int log_n) { return log_n <= kMaxSinglePassLogN ? 1 : (log_n <= 21 ? 2 : 3); }
+inline int plan_1d_passes(int log_n) { return log_n <= kMaxSinglePassLogN ? 1 : (log_n <= 23 ? 2 : 3); }
+
+// Kernels of the two passes of the 2^19..2^23 transforms: per pass the tile
+// kernel family and the tile width (transforms per tile), chosen by measured
+// per-pass time on B200 (512 MiB batches, per pass in ms: the plain strided
+// pass vs the tile kernels; whole transforms 2^19 0.417 -> 0.404,
+// 2^20 0.466 -> 0.425, 2^21 0.510 -> 0.439, 2^22 0.522 -> 0.472,
+// 2^23 (three passes before) 0.542 -> 0.482). Column passes of 512 and 1024
+// take 16 columns per tile (128-byte row segments; the next tile is
+// prefetched into the L2 through a tensor map), 2048 takes 4 columns moved by
+// TMA (its 32-byte segments cost the load/store pipeline a line lookup each;
+// two CTAs per SM); transposed-store row passes of 1024 and 2048 take 8 rows
+// per tile, 4096 takes 4 rows stored by TMA. Below 2^19 the plain kernels,
+// with many CTAs per SM, measured faster; 2^24 and up keep three passes of
+// 128-byte segments (two passes of 4096 with 32-byte segments measured 3 %
+// slower).
+struct TileChoice {
+  TileMode mode;
+  int w;
+};
+inline TileChoice tile_cols_choice(int log_n1) {
+  if (log_n1 == 9 || log_n1 == 10) return {TileMode::Prefetch, 16};
+  if (log_n1 == 11) return {TileMode::Tma, 4};
+  return {TileMode::None, 0};
+}
+inline TileChoice tile_rows_t_choice(int log_n2) {
+  if (log_n2 == 10 || log_n2 == 11) return {TileMode::Prefetch, 8};
+  if (log_n2 == 12) return {TileMode::Tma, 4};
+  return {TileMode::None, 0};
+}
+constexpr int kTileFromLogN = 19;
 
 inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
   PassPlan pl;
@@ -190,6 +234,11 @@ inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
     a.log_m = log_n;
     a.tw_sfu = pass_sfu_supported(l1);
     pl.p[pl.count++] = make_pass(l1, inv, false, PassBuf::In, PassBuf::Ws, a);
+    if (log_n >= kTileFromLogN) {
+      const TileChoice c = tile_cols_choice(l1);
+      pl.p[pl.count - 1].tile = c.mode;
+      pl.p[pl.count - 1].tile_w = c.w;
+    }
     RowsTArgs b{};
     b.nfft = batch * n1;
     b.log_w = l1;
@@ -200,6 +249,11 @@ inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
     b.out_e = n1;
     b.scale = scale;
     pl.p[pl.count++] = make_rows_t(l2, inv, PassBuf::Ws, PassBuf::Out, b);
+    if (log_n >= kTileFromLogN) {
+      const TileChoice c = tile_rows_t_choice(l2);
+      pl.p[pl.count - 1].tile = c.mode;
+      pl.p[pl.count - 1].tile_w = c.w;
+    }
     return pl;
   }
   // Three passes: the row pass (last) gets the largest factor.

@@ -183,9 +183,40 @@ int run_cols_l2(const PassDesc& d, const float2* src, float2* dst, float2* ws) {
   return 0;
 }
 
+// Layout conditions of the tile kernels (launch_tile.cu checks the same at
+// run time and falls back to the plain kernel when one fails; a plan should
+// never need that fallback for its own buffers).
+int check_tile_pass(const PassDesc& d) {
+  if (d.tile == TileMode::None) return 0;
+  if (d.tile_w <= 0) return -80;
+  if (d.kind == PassKind::Pass) {
+    const PassArgs& a = d.pa;
+    if (a.in_c != 1 || a.out_c != 1 || (((int64_t)1 << a.log_w) % d.tile_w) != 0) return -81;
+    if (a.in_o % a.in_e != 0 || a.in_j % a.in_e != 0) return -82;
+    if (d.tile == TileMode::Tma && (a.out_o % a.out_e != 0 || a.out_j % a.out_e != 0)) return -83;
+    if (d.conj_out || a.log_m == 0 || !a.tw_sfu) return -84;  // compiled combinations
+    const bool compiled = (d.tile == TileMode::Prefetch && d.tile_w == 16 &&
+                           (d.log_n == 9 || d.log_n == 10)) ||
+                          (d.tile == TileMode::Tma && d.tile_w == 4 && d.log_n == 11);
+    return compiled ? 0 : -85;
+  }
+  if (d.kind == PassKind::RowsT) {
+    const RowsTArgs& a = d.ra;
+    if ((((int64_t)1 << a.log_w) % d.tile_w) != 0) return -86;
+    if (a.in_c % 2 != 0 || a.in_o % 2 != 0 || a.in_j % 2 != 0) return -87;
+    if (d.tile == TileMode::Tma && (a.out_o % a.out_e != 0 || a.out_j % a.out_e != 0)) return -88;
+    const bool compiled = (d.tile == TileMode::Prefetch && d.tile_w == 8 &&
+                           (d.log_n == 10 || d.log_n == 11)) ||
+                          (d.tile == TileMode::Tma && d.tile_w == 4 && d.log_n == 12);
+    return compiled ? 0 : -89;
+  }
+  return -90;
+}
+
 // One pass of a plan, FFT by FFT (each touches disjoint elements, so in-place
 // passes behave as on the GPU).
 int run_pass(const PassDesc& d, const float2* src, float2* dst, float2* ws) {
+  if (int rc = check_tile_pass(d)) return rc;
   const Tables& tab = tables();
   const int64_t n = (int64_t)1 << d.log_n;
   const float2* stw = tab.stage[d.log_n].data();

@@ -60,7 +60,9 @@ def test_workspace_and_launch_counts(capi):
     assert capi.launch_count(14, 1, 1) == 1
     assert capi.launch_count(15, 1, 1) == 2
     assert capi.launch_count(21, 1, 1) == 2
-    assert capi.launch_count(22, 1, 1) == 3
+    assert capi.launch_count(22, 1, 1) == 2
+    assert capi.launch_count(23, 1, 1) == 2
+    assert capi.launch_count(24, 1, 1) == 3
     assert capi.launch_count(26, 1, 1) == 3
     assert capi.launch_count(10, 16, 2) == 2
     assert capi.launch_count(11, 64, 2) == 2

@@ -37,7 +37,7 @@ def test_single_pass_matches_oracle(emulator, oracle_mod, log_n, direction, norm
 @pytest.mark.parametrize("log_n", [15, 16, 17, 18, 20, 21, 22, 23, 24])
 @pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
 def test_multi_pass_matches_oracle(emulator, oracle_mod, log_n, direction, normalize):
-    # two passes up to 2^21, three passes from 2^22
+    # two passes up to 2^23, three passes from 2^24
     rng = np.random.default_rng(200 + log_n)
     batch = 2 if log_n <= 18 else 1
     x = rand_c64(rng, batch << log_n, "normal")
@@ -48,7 +48,8 @@ def test_multi_pass_matches_oracle(emulator, oracle_mod, log_n, direction, norma
 
 
 def test_pass_counts(emulator):
-    assert [emulator.emu_plan_1d_passes(l) for l in (2, 14, 15, 21, 22, 26)] == [1, 1, 2, 2, 3, 3]
+    assert [emulator.emu_plan_1d_passes(l) for l in (2, 14, 15, 21, 22, 23, 24, 26)] == \
+        [1, 1, 2, 2, 2, 2, 3, 3]
 
 
 @pytest.mark.parametrize("log_n", [2, 3, 4, 5, 6, 8, 10, 11, 12])

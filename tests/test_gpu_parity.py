@@ -139,7 +139,35 @@ def test_four_step(capi, dev, oracle_mod, log_n, direction, normalize):
     assert max_rel_err(got, ref) < TOL
 
 
-@pytest.mark.parametrize("log_n", [15, 18, 21, 22, 24, 26])
+@pytest.mark.parametrize("log_n", [19, 20, 22, 23])
+def test_four_step_unaligned_buffers_use_plain_kernels(capi, dev, oracle_mod, log_n):
+    # The tile kernels of the 2^19..2^23 plans read and write through TMA
+    # tensor maps, which need 16-byte aligned buffers. An input and a
+    # workspace that are 8- but not 16-byte aligned must take the plain
+    # kernels of the same passes and give the same result.
+    rng = np.random.default_rng(4400 + log_n)
+    batch = 2
+    x = rand_c64(rng, batch << log_n, "normal")
+    buf = torch.zeros(x.size + 1, dtype=torch.complex64, device="cuda")
+    buf[1:] = torch.from_numpy(x).to("cuda")
+    assert (buf[1:].data_ptr() % 16) == 8
+    out = torch.empty(x.size, dtype=torch.complex64, device="cuda")
+    ws_bytes = capi.workspace_bytes(log_n, batch, 1)
+    ws = torch.empty(ws_bytes + 8, dtype=torch.uint8, device="cuda")
+    ref = oracle_mod.fft_1d(x, log_n, threads=THREADS)
+    for ws_ptr in (ws.data_ptr(), ws.data_ptr() + 8):
+        capi.fft_1d_ws(dev, buf[1:].data_ptr(), out.data_ptr(), log_n, batch, "forward", False,
+                       ws_ptr, ws_bytes, _stream())
+        torch.cuda.synchronize()
+        assert max_rel_err(out.cpu().numpy(), ref) < TOL
+    aligned = torch.from_numpy(x).to("cuda")
+    capi.fft_1d(dev, aligned.data_ptr(), out.data_ptr(), log_n, batch, "forward", False, _stream())
+    torch.cuda.synchronize()
+    assert max_rel_err(out.cpu().numpy(), ref) < TOL
+    dev.sync()
+
+
+@pytest.mark.parametrize("log_n", [15, 18, 19, 21, 22, 23, 24, 26])
 def test_four_step_accuracy_budget(capi, dev, log_n):
     # The multi-pass 1D takes its four-step twiddle factors from the SFU
     # (sin/cos within ~7e-7 per component instead of a correctly rounded
