@@ -143,10 +143,10 @@ ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* i
       case PassKind::RowsT:
         e = cudaErrorNotSupported;
         if (d.tile != TileMode::None)
-          e = launch_rows_t_tile(d.tile, d.tile_w, d.log_n, d.conj_out, src, dst, stw, d.ra,
-                                 stream);
+          e = launch_rows_t_tile(d.tile, d.tile_w, d.log_n, d.conj_in, d.conj_out, src, dst, stw,
+                                 d.ra, stream);
         if (e == cudaErrorNotSupported)
-          e = launch_rows_t(d.log_n, d.conj_out, src, dst, stw, d.ra, stream);
+          e = launch_rows_t(d.log_n, d.conj_in, d.conj_out, src, dst, stw, d.ra, stream);
         break;
       case PassKind::ColsL2: {
         ColsL2Args a = d.ca;

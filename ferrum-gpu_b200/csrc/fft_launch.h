@@ -58,14 +58,15 @@ cudaError_t launch_pass_tile(TileMode mode, int w, int log_n, bool conj_in, bool
                              bool tw, const float2* in, float2* out, const float2* stage_tw,
                              const PassArgs& args, int* err, cudaStream_t stream);
 
-// Rows of length 2^log_n (4 <= log_n <= 14) stored transposed.
-cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* out,
+// Rows of length 2^log_n (4 <= log_n <= 14) stored transposed; not both
+// conj_in and conj_out.
+cudaError_t launch_rows_t(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
                           const float2* tw, const RowsTArgs& args, cudaStream_t stream);
 // The same in a persistent tile kernel; cudaErrorNotSupported as for
 // launch_pass_tile (the caller then runs launch_rows_t).
-cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_n, bool conj_out, const float2* in,
-                               float2* out, const float2* tw, const RowsTArgs& args,
-                               cudaStream_t stream);
+cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_n, bool conj_in, bool conj_out,
+                               const float2* in, float2* out, const float2* tw,
+                               const RowsTArgs& args, cudaStream_t stream);
 
 // Distributed 2D over peer memory (dist_kernels.cuh); 4 <= log_n <= 14,
 // B = 2^log_b columns per rank. Row FFTs of `nfft` local rows whose output

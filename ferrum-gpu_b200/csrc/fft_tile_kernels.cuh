@@ -119,7 +119,7 @@ struct RowsTTileCfg {
 // rows f = i*W .. i*W + W-1 (W divides 2^log_w). With PF != kPfNone the next
 // tile's rows (contiguous, N*8 bytes each) are prefetched into the L2 with one
 // bulk prefetch per row; the row addresses must then be 16-byte aligned.
-template <int LOGN, int LOGP, int W, bool CONJ_OUT, int PF>
+template <int LOGN, int LOGP, int W, bool CONJ_IN, bool CONJ_OUT, int PF>
 __global__ void __launch_bounds__(RowsTTileCfg<LOGN, LOGP, W>::THREADS,
                                   MinBlocks<RowsTTileCfg<LOGN, LOGP, W>::THREADS, LOGP>::value)
 fft_rows_t_tile_kernel(const float2* in, float2* out, const float2* __restrict__ tw, RowsTArgs a,
@@ -151,7 +151,7 @@ fft_rows_t_tile_kernel(const float2* in, float2* out, const float2* __restrict__
     {
       const float2* src = row_src(tile * W + g) + t;
 #pragma unroll
-      for (int m = 0; m < G::P; ++m) v[m] = ld_stream(src + G::T * m);
+      for (int m = 0; m < G::P; ++m) v[m] = conj_if(ld_stream(src + G::T * m), CONJ_IN);
     }
     // Exchanges within the row's own warps, the last one regrouped so that
     // the lanes run over the tile's rows for the store.
@@ -308,7 +308,7 @@ fft_cols_tma_kernel(const float2* __restrict__ tw, PassArgs a, int64_t ntiles,
 // the output with rows of out_e elements and boxes {W, tile_box_rows(LOGN)};
 // o*out_o + j*out_j must be a multiple of out_e. Row addresses must be
 // 16-byte aligned for the prefetch.
-template <int LOGN, int LOGP, int W, bool CONJ_OUT>
+template <int LOGN, int LOGP, int W, bool CONJ_IN, bool CONJ_OUT>
 __global__ void __launch_bounds__(TmaTileCfg<LOGN, LOGP, W>::THREADS,
                                   MinBlocks<TmaTileCfg<LOGN, LOGP, W>::THREADS, LOGP>::value)
 fft_rows_t_tma_kernel(const float2* in, const float2* __restrict__ tw, RowsTArgs a, int64_t ntiles,
@@ -338,7 +338,7 @@ fft_rows_t_tma_kernel(const float2* in, const float2* __restrict__ tw, RowsTArgs
     {
       const float2* src = row_src(tile * W + g) + t;
 #pragma unroll
-      for (int m = 0; m < G::P; ++m) v[m] = ld_stream(src + G::T * m);
+      for (int m = 0; m < G::P; ++m) v[m] = conj_if(ld_stream(src + G::T * m), CONJ_IN);
     }
     if (threadIdx.x == 0) bulk_wait_read_all();  // the previous tile's store has read the buffer
     __syncthreads();

@@ -42,13 +42,13 @@ cudaError_t cols_l2_dispatch(bool ci, bool co, const float2* in, float2* out, fl
   return cols_l2_impl<L1, L2, W, THREADS, MINB, false, false>(in, out, ws, tw1, tw2, a, slots, s);
 }
 
-template <int LOGN, bool CO>
+template <int LOGN, bool CI, bool CO>
 cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const RowsTArgs& a,
                         cudaStream_t s) {
   constexpr int LOGP = plan_log_p(LOGN);
   constexpr int FPB = cols_fpb(LOGN);
-  using C = RowsTCfg<LOGN, LOGP, FPB, CO>;
-  auto k = fft_rows_t_kernel<LOGN, LOGP, FPB, CO>;
+  using C = RowsTCfg<LOGN, LOGP, FPB, CI, CO>;
+  auto k = fft_rows_t_kernel<LOGN, LOGP, FPB, CI, CO>;
   static std::atomic<uint64_t> smem_done{0};
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
   if (e != cudaSuccess) return e;
@@ -58,13 +58,15 @@ cudaError_t rows_t_impl(const float2* in, float2* out, const float2* tw, const R
   return cudaGetLastError();
 }
 
+// A pass never both conjugates its input and its output.
 template <int LOGN>
-cudaError_t rows_t_dispatch(bool co, const float2* in, float2* out, const float2* tw,
+cudaError_t rows_t_dispatch(bool ci, bool co, const float2* in, float2* out, const float2* tw,
                             const RowsTArgs& a, cudaStream_t s) {
-  if (co) return rows_t_impl<LOGN, true>(in, out, tw, a, s);
-  return rows_t_impl<LOGN, false>(in, out, tw, a, s);
+  if (ci && co) return cudaErrorInvalidValue;
+  if (ci) return rows_t_impl<LOGN, true, false>(in, out, tw, a, s);
+  if (co) return rows_t_impl<LOGN, false, true>(in, out, tw, a, s);
+  return rows_t_impl<LOGN, false, false>(in, out, tw, a, s);
 }
-
 
 template <int LOGN, bool CI>
 cudaError_t rows_scatter_impl(const float2* in, const PeerPtrs& dst, const float2* tw,
@@ -282,12 +284,12 @@ cudaError_t launch_cols_l2(int log_n, bool conj_in, bool conj_out, const float2*
   }
 }
 
-cudaError_t launch_rows_t(int log_n, bool conj_out, const float2* in, float2* out,
+cudaError_t launch_rows_t(int log_n, bool conj_in, bool conj_out, const float2* in, float2* out,
                           const float2* tw, const RowsTArgs& args, cudaStream_t stream) {
   switch (log_n) {
 #define X(L) \
   case L:    \
-    return rows_t_dispatch<L>(conj_out, in, out, tw, args, stream);
+    return rows_t_dispatch<L>(conj_in, conj_out, in, out, tw, args, stream);
     X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14)
 #undef X
     default:

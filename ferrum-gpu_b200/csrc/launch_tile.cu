@@ -142,12 +142,12 @@ bool rows_t_layout_ok(const float2* in, const RowsTArgs& a, int w) {
          a.in_o % 2 == 0 && a.in_j % 2 == 0;
 }
 
-template <int L, int W, bool CO>
+template <int L, int W, bool CI, bool CO>
 cudaError_t rows_t_prefetch_impl(const float2* in, float2* out, const float2* tw,
                                  const RowsTArgs& a, cudaStream_t s) {
   constexpr int LP = plan_log_p(L);
   using C = RowsTTileCfg<L, LP, W>;
-  auto k = fft_rows_t_tile_kernel<L, LP, W, CO, kPfThreads>;
+  auto k = fft_rows_t_tile_kernel<L, LP, W, CI, CO, kPfThreads>;
   static std::atomic<uint64_t> smem_done{0};
   if (!rows_t_layout_ok(in, a, W)) return cudaErrorNotSupported;
   cudaError_t e = ensure_smem(k, C::SMEM_BYTES, smem_done);
@@ -160,12 +160,12 @@ cudaError_t rows_t_prefetch_impl(const float2* in, float2* out, const float2* tw
   return cudaGetLastError();
 }
 
-template <int L, int W, bool CO>
+template <int L, int W, bool CI, bool CO>
 cudaError_t rows_t_tma_impl(const float2* in, float2* out, const float2* tw, const RowsTArgs& a,
                             cudaStream_t s) {
   constexpr int LP = plan_log_p(L);
   using C = TmaTileCfg<L, LP, W>;
-  auto k = fft_rows_t_tma_kernel<L, LP, W, CO>;
+  auto k = fft_rows_t_tma_kernel<L, LP, W, CI, CO>;
   static std::atomic<uint64_t> smem_done{0};
   if (!rows_t_layout_ok(in, a, W) || a.out_o % a.out_e != 0 || a.out_j % a.out_e != 0)
     return cudaErrorNotSupported;
@@ -208,20 +208,34 @@ cudaError_t launch_pass_tile(TileMode mode, int w, int log_n, bool conj_in, bool
   return cudaErrorNotSupported;
 }
 
-cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_n, bool conj_out, const float2* in,
-                               float2* out, const float2* tw, const RowsTArgs& a,
-                               cudaStream_t stream) {
+template <int L, int W>
+cudaError_t rows_t_prefetch_dispatch(bool ci, bool co, const float2* in, float2* out,
+                                     const float2* tw, const RowsTArgs& a, cudaStream_t s) {
+  if (ci) return rows_t_prefetch_impl<L, W, true, false>(in, out, tw, a, s);
+  if (co) return rows_t_prefetch_impl<L, W, false, true>(in, out, tw, a, s);
+  return rows_t_prefetch_impl<L, W, false, false>(in, out, tw, a, s);
+}
+
+template <int L, int W>
+cudaError_t rows_t_tma_dispatch(bool ci, bool co, const float2* in, float2* out, const float2* tw,
+                                const RowsTArgs& a, cudaStream_t s) {
+  if (ci) return rows_t_tma_impl<L, W, true, false>(in, out, tw, a, s);
+  if (co) return rows_t_tma_impl<L, W, false, true>(in, out, tw, a, s);
+  return rows_t_tma_impl<L, W, false, false>(in, out, tw, a, s);
+}
+
+cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_n, bool conj_in, bool conj_out,
+                               const float2* in, float2* out, const float2* tw,
+                               const RowsTArgs& a, cudaStream_t stream) {
+  // Compiled: the last passes of the 2^19..2^23 plans and both passes of the
+  // 2D plans for N = 1024..4096; no pass conjugates both ways.
+  if (conj_in && conj_out) return cudaErrorNotSupported;
   if (mode == TileMode::Prefetch && w == 8) {
-    if (log_n == 10)
-      return conj_out ? rows_t_prefetch_impl<10, 8, true>(in, out, tw, a, stream)
-                      : rows_t_prefetch_impl<10, 8, false>(in, out, tw, a, stream);
-    if (log_n == 11)
-      return conj_out ? rows_t_prefetch_impl<11, 8, true>(in, out, tw, a, stream)
-                      : rows_t_prefetch_impl<11, 8, false>(in, out, tw, a, stream);
+    if (log_n == 10) return rows_t_prefetch_dispatch<10, 8>(conj_in, conj_out, in, out, tw, a, stream);
+    if (log_n == 11) return rows_t_prefetch_dispatch<11, 8>(conj_in, conj_out, in, out, tw, a, stream);
   }
   if (mode == TileMode::Tma && w == 4 && log_n == 12)
-    return conj_out ? rows_t_tma_impl<12, 4, true>(in, out, tw, a, stream)
-                    : rows_t_tma_impl<12, 4, false>(in, out, tw, a, stream);
+    return rows_t_tma_dispatch<12, 4>(conj_in, conj_out, in, out, tw, a, stream);
   return cudaErrorNotSupported;
 }
 

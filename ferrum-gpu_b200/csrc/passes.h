@@ -13,13 +13,16 @@
 //       1  DFT over n1, times W_{N1 N2}^(n2*k1);
 //       2  DFT over n2, times W_N^(n3*(k1 + N1*k2));
 //       3  DFT over n3 (rows), stored to X[k1 + N1*k2 + N1*N2*k3].
-//   * 2D N x N, N <= 2048: row pass, then one column pass in place (N = 2048
-//     reads 32-byte row segments, still near full DRAM efficiency on B200).
-//   * 2D, N >= 4096: columns first as two sub-passes (N = A*B, row a + A*b:
+//   * 2D N x N, N <= 512: row pass, then one column pass in place.
+//   * 2D, N = 1024..4096: two transposed-row passes through a workspace
+//     (rows of each image stored transposed, then the rows of that stored
+//     transposed back), in the persistent tile kernels.
+//   * 2D, N >= 8192: columns first as two sub-passes (N = A*B, row a + A*b:
 //     DFT over b times W_N^(a*kb), then DFT over a stored to row kb + B*ka),
-//     run by one persistent kernel that keeps the intermediate of each tile of
-//     columns in an L2-resident scratch slot (fft_cols_l2_kernel), then the
-//     row pass in place, which also applies the inverse's conjugate and scale.
+//     then the row pass, which also applies the inverse's conjugate and
+//     scale. (The fused two-sub-pass column kernel, fft_cols_l2_kernel, keeps
+//     the intermediate of each tile of 4096-point columns in an L2-resident
+//     scratch slot; the distributed transform's column passes use it.)
 // The index identities are the Cooley-Tukey splits; the reference's CPU
 // Stockham (crates/ferrum-gpu-fft/src/cpu.rs) defines the results they must
 // reproduce.
@@ -112,10 +115,12 @@ inline PassDesc make_pass(int log_n, bool ci, bool co, PassBuf src, PassBuf dst,
   return d;
 }
 
-inline PassDesc make_rows_t(int log_n, bool co, PassBuf src, PassBuf dst, const RowsTArgs& a) {
+inline PassDesc make_rows_t(int log_n, bool co, PassBuf src, PassBuf dst, const RowsTArgs& a,
+                            bool ci = false) {
   PassDesc d{};
   d.kind = PassKind::RowsT;
   d.log_n = log_n;
+  d.conj_in = ci;
   d.conj_out = co;
   d.src = src;
   d.dst = dst;
@@ -328,11 +333,53 @@ inline void plan_columns(PassPlan& pl, int log_n, int log_width, int64_t ld, int
   pl.p[pl.count++] = make_pass(la, false, co, mid, dst, a2);
 }
 
+// 2D lengths run as two transposed-row passes (2^log_n x 2^log_n images):
+// per pass the tile kernel and rows per tile. Measured on B200 for 512 MiB of
+// images, forward (ms): N = 1024 0.394 -> 0.381, 2048 0.465 -> 0.397,
+// 4096 0.471 -> 0.434 against a row pass plus column passes; up to 512 the
+// row pass plus one column pass is faster (more CTAs per SM), and from 8192
+// a tile of 4 rows no longer fits one SM's shared memory.
+inline TileChoice tile_2d_choice(int log_n) {
+  if (log_n == 10 || log_n == 11) return {TileMode::Prefetch, 8};
+  if (log_n == 12) return {TileMode::Tma, 4};
+  return {TileMode::None, 0};
+}
+
+inline RowsTArgs rows_t_2d_args(int log_n, int64_t batch, float scale) {
+  const int64_t n = (int64_t)1 << log_n;
+  RowsTArgs b{};
+  b.nfft = batch * n;
+  b.log_w = log_n;
+  b.log_j = 0;
+  b.in_o = n * n;
+  b.in_c = n;
+  b.out_o = n * n;
+  b.out_e = n;
+  b.scale = scale;
+  return b;
+}
+
 inline PassPlan plan_2d(int log_n, int64_t batch, bool inv, bool normalize) {
   PassPlan pl;
   const int64_t n = (int64_t)1 << log_n;
   // cpu_2d.rs:56-62: one 1/(n*n) scale computed in float.
   const float scale = (inv && normalize) ? 1.0f / ((float)n * (float)n) : 1.0f;
+  const TileChoice tc = tile_2d_choice(log_n);
+  if (tc.mode != TileMode::None) {
+    // Row FFTs of every image stored transposed into the workspace (the
+    // transposed image's rows are the columns), then row FFTs of those stored
+    // transposed back: the columns' FFTs in natural layout.
+    pl.ws_elems = batch * n * n;
+    pl.p[pl.count++] = make_rows_t(log_n, false, PassBuf::In, PassBuf::Ws,
+                                   rows_t_2d_args(log_n, batch, 1.0f), inv);
+    pl.p[pl.count++] = make_rows_t(log_n, inv, PassBuf::Ws, PassBuf::Out,
+                                   rows_t_2d_args(log_n, batch, scale));
+    for (int i = 0; i < 2; ++i) {
+      pl.p[i].tile = tc.mode;
+      pl.p[i].tile_w = tc.w;
+    }
+    return pl;
+  }
   if (log_n <= kMaxOnePassColumnLogN) {
     pl.p[pl.count++] = make_rows(log_n, batch * n, inv, false, 1.0f, PassBuf::In, PassBuf::Out);
     plan_columns(pl, log_n, log_n, n, batch, n * n, false, inv, scale, PassBuf::Out, PassBuf::Out,

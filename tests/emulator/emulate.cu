@@ -265,12 +265,14 @@ int run_pass(const PassDesc& d, const float2* src, float2* dst, float2* ws) {
       return run_cols_l2(d, src, dst, ws);
     case PassKind::RowsT: {
       const RowsTArgs& a = d.ra;
-      if (d.conj_in || d.log_n < 4) return -61;  // fft_rows_t_kernel: no conj_in, 4 <= log_n <= 14
+      // fft_rows_t_kernel: 4 <= log_n <= 14, not both conj_in and conj_out
+      if ((d.conj_in && d.conj_out) || d.log_n < 4) return -61;
       for (int64_t f = 0; f < a.nfft; ++f) {
         int64_t o, j, c;
         pass_index(f, a.log_w, a.log_j, o, j, c);
         const int64_t ib = o * a.in_o + j * a.in_j + c * a.in_c, ob = o * a.out_o + j * a.out_j + c;
-        if (int rc = run_group(d.log_n, src + ib, x.data(), stw)) return rc;
+        for (int64_t e = 0; e < n; ++e) x[e] = conj_if(src[ib + e], d.conj_in);
+        if (int rc = run_group(d.log_n, x.data(), x.data(), stw)) return rc;
         for (int64_t k = 0; k < n; ++k) dst[ob + k * a.out_e] = epi(x[k], d.conj_out, a.scale);
       }
       return 0;

@@ -49,11 +49,12 @@ def test_workspace_and_launch_counts(capi):
     assert capi.workspace_bytes(12, 65536, 1) == 0
     assert capi.workspace_bytes(20, 64, 1) == (1 << 20) * 64 * 8
     assert capi.workspace_bytes(24, 4, 1) == (1 << 24) * 4 * 8
-    # 2D up to 1024^2: row pass + one column pass in place; from 2048^2 the
-    # columns run as two sub-passes through an image-sized workspace.
-    assert capi.workspace_bytes(10, 16, 2) == 0
-    # 2D N >= 4096: the fused column kernel's L2 scratch slots (slots x W x N)
-    assert capi.workspace_bytes(12, 16, 2) == 148 * 8 * 4096 * 8
+    # 2D up to 512^2: row pass + one column pass in place, no workspace;
+    # 1024^2..4096^2: two transposed-row passes through an image-sized
+    # workspace; from 8192^2 two column sub-passes through one.
+    assert capi.workspace_bytes(9, 16, 2) == 0
+    assert capi.workspace_bytes(10, 16, 2) == 16 * (1 << 20) * 8
+    assert capi.workspace_bytes(12, 16, 2) == 16 * (1 << 24) * 8
     assert capi.workspace_bytes(13, 4, 2) == 4 * (1 << 26) * 8   # separate sub-passes
     assert capi.workspace_bytes(14, 1, 2) == (1 << 28) * 8   # separate sub-passes
     assert capi.launch_count(10, 256, 1) == 1
@@ -66,7 +67,7 @@ def test_workspace_and_launch_counts(capi):
     assert capi.launch_count(26, 1, 1) == 3
     assert capi.launch_count(10, 16, 2) == 2
     assert capi.launch_count(11, 64, 2) == 2
-    assert capi.workspace_bytes(11, 64, 2) == 0
+    assert capi.launch_count(9, 64, 2) == 2
     assert capi.launch_count(12, 16, 2) == 2
     assert capi.launch_count(14, 1, 2) == 3
 
