@@ -356,15 +356,7 @@ struct ColsL2Cfg {
   static constexpr int64_t SLOT = (int64_t)W << (L1 + L2);  // complex values per CTA
 };
 
-// DISCARD: once a tile's slot has been read for the last time, its L2 lines
-// are dropped (`discard.global.L2`) instead of being written back to HBM when
-// they are evicted; the slot is rewritten before it is read again. Needs a
-// 128-byte aligned workspace (checked at run time; otherwise nothing is
-// discarded). PF: the next tile's input is prefetched into the L2 (one
-// bulk prefetch per W*8-byte row segment) while the current tile is
-// transformed.
-template <int L1, int L2, int W, int THREADS, int MINB, bool CONJ_IN, bool CONJ_OUT,
-          bool DISCARD = false, bool PF = false>
+template <int L1, int L2, int W, int THREADS, int MINB, bool CONJ_IN, bool CONJ_OUT>
 __global__ void __launch_bounds__(THREADS, MINB)
 fft_cols_l2_kernel(const float2* in, float2* out, float2* ws, const float2* __restrict__ tw1,
                    const float2* __restrict__ tw2, ColsL2Args a) {
@@ -378,22 +370,8 @@ fft_cols_l2_kernel(const float2* in, float2* out, float2* ws, const float2* __re
   float2* slot = ws + (int64_t)blockIdx.x * C::SLOT;
   const int cl = threadIdx.x % W;
   const int64_t tile_mask = ((int64_t)1 << a.log_tiles_per_img) - 1;
-  const bool discard = DISCARD && (((uintptr_t)slot & 127u) == 0);
   for (int64_t tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
     const int64_t base = (tile >> a.log_tiles_per_img) * a.img_stride + (tile & tile_mask) * W + cl;
-    if constexpr (PF) {
-      const int64_t next = tile + gridDim.x;
-      if (next < a.tiles) {
-        const float2* nb = in + (next >> a.log_tiles_per_img) * a.img_stride + (next & tile_mask) * W;
-        if ((((uintptr_t)nb | (uintptr_t)(a.ld * 8)) & 15u) == 0) {
-#pragma unroll 1
-          for (int e = threadIdx.x; e < (A * B); e += THREADS)
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(nb + e * a.ld),
-                         "r"((uint32_t)(W * sizeof(float2)))
-                         : "memory");
-        }
-      }
-    }
     {
       const int t1 = (threadIdx.x / W) % C::G1::T, u1 = threadIdx.x / (W * C::G1::T);
       float2* sm1 = smem + (u1 * W + cl) * C::RS1;
@@ -434,18 +412,6 @@ fft_cols_l2_kernel(const float2* in, float2* out, float2* ws, const float2* __re
       }
     }
     __syncthreads();  // every read of the slot is done before the next tile rewrites it
-    if constexpr (DISCARD) {
-      if (discard) {
-        // The slot is dead until the next tile rewrites it: drop its lines.
-        constexpr int kLines = (int)(C::SLOT * sizeof(float2) / 128);
-#pragma unroll 1
-        for (int i = threadIdx.x; i < kLines; i += THREADS)
-          asm volatile("discard.global.L2 [%0], 128;" ::"l"(reinterpret_cast<char*>(slot) + 128 * i)
-                       : "memory");
-        __threadfence_block();
-        __syncthreads();  // the discards are ordered before the next tile's slot stores
-      }
-    }
   }
 }
 

@@ -51,12 +51,12 @@ def test_workspace_and_launch_counts(capi):
     assert capi.workspace_bytes(24, 4, 1) == (1 << 24) * 4 * 8
     # 2D up to 512^2: row pass + one column pass in place, no workspace;
     # 1024^2..4096^2: two transposed-row passes through an image-sized
-    # workspace; from 8192^2 two column sub-passes through one.
+    # workspace; from 8192^2 two column sub-passes and the row pass.
     assert capi.workspace_bytes(9, 16, 2) == 0
     assert capi.workspace_bytes(10, 16, 2) == 16 * (1 << 20) * 8
     assert capi.workspace_bytes(12, 16, 2) == 16 * (1 << 24) * 8
-    assert capi.workspace_bytes(13, 4, 2) == 4 * (1 << 26) * 8   # separate sub-passes
-    assert capi.workspace_bytes(14, 1, 2) == (1 << 28) * 8   # separate sub-passes
+    assert capi.workspace_bytes(13, 4, 2) == 4 * (1 << 26) * 8
+    assert capi.workspace_bytes(14, 1, 2) == (1 << 28) * 8
     assert capi.launch_count(10, 256, 1) == 1
     assert capi.launch_count(14, 1, 1) == 1
     assert capi.launch_count(15, 1, 1) == 2
@@ -70,6 +70,7 @@ def test_workspace_and_launch_counts(capi):
     assert capi.launch_count(9, 64, 2) == 2
     assert capi.launch_count(12, 16, 2) == 2
     assert capi.launch_count(14, 1, 2) == 3
+    assert capi.launch_count(13, 4, 2) == 3
 
 
 @pytest.mark.parametrize("log_n,batch,kind", [(1, 1, 1), (27, 1, 1), (10, 0, 1), (15, 1, 2),
