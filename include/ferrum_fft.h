@@ -44,8 +44,14 @@ enum {
 
 enum { FERRUM_FORWARD = 1, FERRUM_INVERSE = -1 };
 
-/* Supported sizes. 1D lengths up to 2^14 run as one HBM pass; 2^15..2^26 run
- * the two-pass four-step. 2D images are N x N with N up to 2^14. */
+/* Supported sizes. 1D lengths up to 2^14 run as one HBM pass; 2^15..2^23 run
+ * the two-pass four-step and 2^24..2^26 a three-pass split. 2D images are
+ * N x N with N up to 2^14. Every call covers at most 2^36 complex values
+ * (N * batch, or N * N * batch for 2D); larger requests return
+ * FERRUM_ERR_INVALID_ARG. Buffers need 8-byte alignment; the fastest
+ * multi-pass and 2D kernels read and write through TMA and need 16-byte
+ * aligned buffers (8-byte aligned ones run slower kernels with the same
+ * results). */
 #define FERRUM_MIN_LOG_N 2
 #define FERRUM_MAX_LOG_N_SINGLE_PASS 14
 #define FERRUM_MAX_LOG_N_1D 26
@@ -74,7 +80,8 @@ ferrum_status ferrum_device_ordinal(const ferrum_device *dev, int *ordinal);
  * Device-resident form of `fft_1d_c2c_pow2` / `run_fft_flat_with_device`
  * (crates/ferrum-gpu-py/src/lib.rs:445-504, :86-250); log_n in [2, 26].
  * Lengths above 2^14 need a workspace of N*batch*8 bytes, taken from the
- * device's stream-ordered memory pool. */
+ * device's stream-ordered memory pool. A kernel's bounded wait that runs out
+ * sets a device flag that ferrum_device_sync reports as FERRUM_ERR_TIMEOUT. */
 ferrum_status ferrum_fft_1d_c2c_pow2(ferrum_device *dev, const void *in_dev, void *out_dev,
                                      int log_n, size_t batch, int direction, int normalize,
                                      void *stream);
@@ -105,8 +112,10 @@ ferrum_status ferrum_fft_1d_c2c_pow2_noalloc(ferrum_device *dev, const void *in_
 /* Batched 2D C2C on device memory: `batch` images of N x N, N = 2^log_n,
  * log_n in [2, 14]. Replaces `fft_2d_c2c_pow2` / `run_fft_2d_flat`
  * (crates/ferrum-gpu-py/src/lib.rs:527-588, :273-375); the reference's 2D takes
- * one image and log_n in [4, 12]. Two HBM passes: row FFTs, then column FFTs
- * in place. */
+ * one image and log_n in [4, 12]. Up to N = 512 a row pass and a column pass
+ * in place; N = 1024..4096 two transposed-row passes through an image-sized
+ * workspace; N >= 8192 two column sub-passes and a row pass (workspace from
+ * the device's stream-ordered pool). */
 ferrum_status ferrum_fft_2d_c2c_pow2(ferrum_device *dev, const void *in_dev, void *out_dev,
                                      int log_n, size_t batch, int direction, int normalize,
                                      void *stream);
