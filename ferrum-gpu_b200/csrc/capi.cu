@@ -58,6 +58,12 @@ DeviceGuard::~DeviceGuard() {
 const float2* stage_table(const ferrum_device* dev, int log_n) {
   return dev->tables + dev->stage_off[log_n];
 }
+const float2* stage_table_p(const ferrum_device* dev, int log_n, int log_p) {
+  if (log_p == plan_log_p(log_n)) return stage_table(dev, log_n);
+  if (log_p == 5 && tile_p32_table(log_n) && dev->stage32_off[log_n] >= 0)
+    return dev->tables + dev->stage32_off[log_n];
+  return nullptr;
+}
 const float2* tw4_lo_table(const ferrum_device* dev, int log_n) {
   return dev->tables + dev->tw4_lo_off[log_n];
 }
@@ -134,8 +140,9 @@ ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* i
         }
         e = cudaErrorNotSupported;
         if (d.tile != TileMode::None)
-          e = launch_pass_tile(d.tile, d.tile_w, d.log_n, d.conj_in, d.conj_out, a.log_m > 0, src,
-                               dst, stw, a, dev->err_flag, stream);
+          e = launch_pass_tile(d.tile, d.tile_w, tile_log_p(d), d.log_n, d.conj_in, d.conj_out,
+                               a.log_m > 0, src, dst, stage_table_p(dev, d.log_n, tile_log_p(d)),
+                               a, dev->err_flag, stream);
         if (e == cudaErrorNotSupported)
           e = launch_pass(d.log_n, d.conj_in, d.conj_out, a.log_m > 0, src, dst, stw, a, stream);
         break;
@@ -143,8 +150,9 @@ ferrum_status run_plan(ferrum_device* dev, const PassPlan& plan, const float2* i
       case PassKind::RowsT:
         e = cudaErrorNotSupported;
         if (d.tile != TileMode::None)
-          e = launch_rows_t_tile(d.tile, d.tile_w, d.log_n, d.conj_in, d.conj_out, src, dst, stw,
-                                 d.ra, stream);
+          e = launch_rows_t_tile(d.tile, d.tile_w, tile_log_p(d), d.log_n, d.conj_in, d.conj_out,
+                                 src, dst, stage_table_p(dev, d.log_n, tile_log_p(d)), d.ra,
+                                 stream);
         if (e == cudaErrorNotSupported)
           e = launch_rows_t(d.log_n, d.conj_in, d.conj_out, src, dst, stw, d.ra, stream);
         break;
@@ -221,12 +229,17 @@ ferrum_status ferrum_device_create(int ordinal, ferrum_device** out) {
   std::vector<float2> host;
   auto* dev = new ferrum_device();
   dev->ordinal = ordinal;
-  for (int l = 0; l <= kMaxSinglePassLogN; ++l) dev->stage_off[l] = -1;
+  for (int l = 0; l <= kMaxSinglePassLogN; ++l) dev->stage_off[l] = dev->stage32_off[l] = -1;
   for (int l = 0; l <= kMaxLogN; ++l) dev->tw4_lo_off[l] = dev->tw4_hi_off[l] = -1;
   for (int l = 2; l <= kMaxSinglePassLogN; ++l) {
     dev->stage_off[l] = (int64_t)host.size();
     append_stage_tables(host, l);
     host.push_back(make_float2(1.f, 0.f));  // keeps every offset valid for 1-stage plans
+    if (tile_p32_table(l)) {
+      dev->stage32_off[l] = (int64_t)host.size();
+      append_stage_tables(host, l, 5);
+      host.push_back(make_float2(1.f, 0.f));
+    }
   }
   for (int l = 1; l <= kMaxLogN; ++l) {
     std::vector<float2> lo, hi;

@@ -50,13 +50,15 @@ cudaError_t launch_cols_l2(int log_n, bool conj_in, bool conj_out, const float2*
                            cudaStream_t stream);
 
 // The same strided pass in a persistent tile kernel (launch_tile.cu) of the
-// given family and tile width; cudaErrorNotSupported when that kernel is not
+// given family, tile width and values per thread (2^log_p; `stage_tw` is the
+// stage table for that split, stage_table_p); cudaErrorNotSupported when that kernel is not
 // compiled for these arguments or the layout does not meet its conditions
 // (the caller then runs launch_pass). `err` is the device flag of the TMA
 // kernel's bounded waits.
-cudaError_t launch_pass_tile(TileMode mode, int w, int log_n, bool conj_in, bool conj_out,
-                             bool tw, const float2* in, float2* out, const float2* stage_tw,
-                             const PassArgs& args, int* err, cudaStream_t stream);
+cudaError_t launch_pass_tile(TileMode mode, int w, int log_p, int log_n, bool conj_in,
+                             bool conj_out, bool tw, const float2* in, float2* out,
+                             const float2* stage_tw, const PassArgs& args, int* err,
+                             cudaStream_t stream);
 
 // Rows of length 2^log_n (4 <= log_n <= 14) stored transposed; not both
 // conj_in and conj_out.
@@ -64,8 +66,8 @@ cudaError_t launch_rows_t(int log_n, bool conj_in, bool conj_out, const float2* 
                           const float2* tw, const RowsTArgs& args, cudaStream_t stream);
 // The same in a persistent tile kernel; cudaErrorNotSupported as for
 // launch_pass_tile (the caller then runs launch_rows_t).
-cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_n, bool conj_in, bool conj_out,
-                               const float2* in, float2* out, const float2* tw,
+cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_p, int log_n, bool conj_in,
+                               bool conj_out, const float2* in, float2* out, const float2* tw,
                                const RowsTArgs& args, cudaStream_t stream);
 
 // Distributed 2D over peer memory (dist_kernels.cuh); 4 <= log_n <= 14,

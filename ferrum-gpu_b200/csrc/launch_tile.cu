@@ -91,10 +91,9 @@ cudaError_t resident_grid(K kernel, int threads, size_t smem, int64_t ntiles, in
   return cudaSuccess;
 }
 
-template <int L, int W, bool CI, int TW>
+template <int L, int LP, int W, bool CI, int TW>
 cudaError_t cols_prefetch_impl(const float2* in, float2* out, const float2* tw, const PassArgs& a,
                                cudaStream_t s) {
-  constexpr int LP = plan_log_p(L);
   using C = ColsTileCfg<L, LP, W>;
   auto k = fft_cols_tile_kernel<L, LP, W, CI, false, TW, kPfTensor>;
   static std::atomic<uint64_t> smem_done{0};
@@ -142,10 +141,9 @@ bool rows_t_layout_ok(const float2* in, const RowsTArgs& a, int w) {
          a.in_o % 2 == 0 && a.in_j % 2 == 0;
 }
 
-template <int L, int W, bool CI, bool CO>
+template <int L, int LP, int W, bool CI, bool CO>
 cudaError_t rows_t_prefetch_impl(const float2* in, float2* out, const float2* tw,
                                  const RowsTArgs& a, cudaStream_t s) {
-  constexpr int LP = plan_log_p(L);
   using C = RowsTTileCfg<L, LP, W>;
   auto k = fft_rows_t_tile_kernel<L, LP, W, CI, CO, kPfThreads>;
   static std::atomic<uint64_t> smem_done{0};
@@ -188,32 +186,33 @@ cudaError_t rows_t_tma_impl(const float2* in, float2* out, const float2* tw, con
 
 }  // namespace
 
-cudaError_t launch_pass_tile(TileMode mode, int w, int log_n, bool conj_in, bool conj_out,
-                             bool tw, const float2* in, float2* out, const float2* stage_tw,
-                             const PassArgs& a, int* err, cudaStream_t stream) {
+cudaError_t launch_pass_tile(TileMode mode, int w, int log_p, int log_n, bool conj_in,
+                             bool conj_out, bool tw, const float2* in, float2* out,
+                             const float2* stage_tw, const PassArgs& a, int* err,
+                             cudaStream_t stream) {
   // Compiled: the column passes of the 2^19..2^23 plans (SFU twiddle, no
   // conjugated output).
-  if (conj_out || !tw || !a.tw_sfu) return cudaErrorNotSupported;
-  if (mode == TileMode::Prefetch && w == 16) {
+  if (conj_out || !tw || !a.tw_sfu || stage_tw == nullptr) return cudaErrorNotSupported;
+  if (mode == TileMode::Prefetch && w == 16 && log_p == 5) {
     if (log_n == 9)
-      return conj_in ? cols_prefetch_impl<9, 16, true, 2>(in, out, stage_tw, a, stream)
-                     : cols_prefetch_impl<9, 16, false, 2>(in, out, stage_tw, a, stream);
+      return conj_in ? cols_prefetch_impl<9, 5, 16, true, 2>(in, out, stage_tw, a, stream)
+                     : cols_prefetch_impl<9, 5, 16, false, 2>(in, out, stage_tw, a, stream);
     if (log_n == 10)
-      return conj_in ? cols_prefetch_impl<10, 16, true, 2>(in, out, stage_tw, a, stream)
-                     : cols_prefetch_impl<10, 16, false, 2>(in, out, stage_tw, a, stream);
+      return conj_in ? cols_prefetch_impl<10, 5, 16, true, 2>(in, out, stage_tw, a, stream)
+                     : cols_prefetch_impl<10, 5, 16, false, 2>(in, out, stage_tw, a, stream);
   }
-  if (mode == TileMode::Tma && w == 4 && log_n == 11)
+  if (mode == TileMode::Tma && w == 4 && log_n == 11 && log_p == 4)
     return conj_in ? cols_tma_impl<11, 4, true, 2>(in, out, stage_tw, a, err, stream)
                    : cols_tma_impl<11, 4, false, 2>(in, out, stage_tw, a, err, stream);
   return cudaErrorNotSupported;
 }
 
-template <int L, int W>
+template <int L, int LP, int W>
 cudaError_t rows_t_prefetch_dispatch(bool ci, bool co, const float2* in, float2* out,
                                      const float2* tw, const RowsTArgs& a, cudaStream_t s) {
-  if (ci) return rows_t_prefetch_impl<L, W, true, false>(in, out, tw, a, s);
-  if (co) return rows_t_prefetch_impl<L, W, false, true>(in, out, tw, a, s);
-  return rows_t_prefetch_impl<L, W, false, false>(in, out, tw, a, s);
+  if (ci) return rows_t_prefetch_impl<L, LP, W, true, false>(in, out, tw, a, s);
+  if (co) return rows_t_prefetch_impl<L, LP, W, false, true>(in, out, tw, a, s);
+  return rows_t_prefetch_impl<L, LP, W, false, false>(in, out, tw, a, s);
 }
 
 template <int L, int W>
@@ -224,17 +223,19 @@ cudaError_t rows_t_tma_dispatch(bool ci, bool co, const float2* in, float2* out,
   return rows_t_tma_impl<L, W, false, false>(in, out, tw, a, s);
 }
 
-cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_n, bool conj_in, bool conj_out,
-                               const float2* in, float2* out, const float2* tw,
+cudaError_t launch_rows_t_tile(TileMode mode, int w, int log_p, int log_n, bool conj_in,
+                               bool conj_out, const float2* in, float2* out, const float2* tw,
                                const RowsTArgs& a, cudaStream_t stream) {
   // Compiled: the last passes of the 2^19..2^23 plans and both passes of the
   // 2D plans for N = 1024..4096; no pass conjugates both ways.
-  if (conj_in && conj_out) return cudaErrorNotSupported;
+  if ((conj_in && conj_out) || tw == nullptr) return cudaErrorNotSupported;
   if (mode == TileMode::Prefetch && w == 8) {
-    if (log_n == 10) return rows_t_prefetch_dispatch<10, 8>(conj_in, conj_out, in, out, tw, a, stream);
-    if (log_n == 11) return rows_t_prefetch_dispatch<11, 8>(conj_in, conj_out, in, out, tw, a, stream);
+    if (log_n == 10 && log_p == 5)
+      return rows_t_prefetch_dispatch<10, 5, 8>(conj_in, conj_out, in, out, tw, a, stream);
+    if (log_n == 11 && log_p == 4)
+      return rows_t_prefetch_dispatch<11, 4, 8>(conj_in, conj_out, in, out, tw, a, stream);
   }
-  if (mode == TileMode::Tma && w == 4 && log_n == 12)
+  if (mode == TileMode::Tma && w == 4 && log_n == 12 && log_p == 4)
     return rows_t_tma_dispatch<12, 4>(conj_in, conj_out, in, out, tw, a, stream);
   return cudaErrorNotSupported;
 }

@@ -61,6 +61,11 @@ FERRUM_HD constexpr int64_t plan_tw_count(int log_n, int log_p) {
          plan_stage_tw_count(log_n, log_p, plan_num_stages(log_n, log_p) - 1);
 }
 
+// Lengths whose plan takes 16 values per thread but for which the device also
+// holds stage tables with 32 (tile kernels that run them with 32 values per
+// thread: fewer exchanges, measured faster at these lengths).
+FERRUM_HD constexpr bool tile_p32_table(int log_n) { return log_n >= 9 && log_n <= 12; }
+
 // Largest single-pass length (one HBM read + one HBM write per element).
 constexpr int kMaxSinglePassLogN = 14;
 // Largest 1D length (four-step, two passes).

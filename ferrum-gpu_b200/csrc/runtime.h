@@ -17,6 +17,9 @@ struct ferrum_device {
   float2* tables = nullptr;
   size_t table_entries = 0;
   int64_t stage_off[ferrum::kMaxSinglePassLogN + 1] = {};  // per log_n, -1 if absent
+  // Stage tables with 32 values per thread for the lengths whose plan uses
+  // 16 (the tile kernels that run them with 32; ferrum::kTileP32Lengths).
+  int64_t stage32_off[ferrum::kMaxSinglePassLogN + 1] = {};
   int64_t tw4_lo_off[ferrum::kMaxLogN + 1] = {};
   int64_t tw4_hi_off[ferrum::kMaxLogN + 1] = {};
   cudaMemPool_t pool = nullptr;  // stream-ordered workspace pool
@@ -54,6 +57,9 @@ class DeviceGuard {
 };
 
 const float2* stage_table(const ferrum_device* dev, int log_n);
+// Stage table of length 2^log_n with 2^log_p values per thread (log_p 4 or
+// 5; NULL where the device holds none).
+const float2* stage_table_p(const ferrum_device* dev, int log_n, int log_p);
 const float2* tw4_lo_table(const ferrum_device* dev, int log_n);
 const float2* tw4_hi_table(const ferrum_device* dev, int log_n);
 

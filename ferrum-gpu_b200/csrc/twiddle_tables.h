@@ -18,10 +18,11 @@ inline float2 root_of_unity(int64_t e, int64_t m) {
   return make_float2((float)cos(a), (float)sin(a));
 }
 
-// Stage tables of a length-2^log_n plan, concatenated in stage order
-// (layout documented in plan.h).
-inline void append_stage_tables(std::vector<float2>& out, int log_n) {
-  const int lp = plan_log_p(log_n);
+// Stage tables of a length-2^log_n plan with 2^lp values per thread
+// (default plan_log_p(log_n)), concatenated in stage order (layout
+// documented in plan.h).
+inline void append_stage_tables(std::vector<float2>& out, int log_n, int lp = -1) {
+  if (lp < 0) lp = plan_log_p(log_n);
   const int stages = plan_num_stages(log_n, lp);
   for (int s = 1; s < stages; ++s) {
     const int lr = plan_log_radix(log_n, lp, s);

@@ -195,9 +195,11 @@ int check_tile_pass(const PassDesc& d) {
     if (a.in_o % a.in_e != 0 || a.in_j % a.in_e != 0) return -82;
     if (d.tile == TileMode::Tma && (a.out_o % a.out_e != 0 || a.out_j % a.out_e != 0)) return -83;
     if (d.conj_out || a.log_m == 0 || !a.tw_sfu) return -84;  // compiled combinations
-    const bool compiled = (d.tile == TileMode::Prefetch && d.tile_w == 16 &&
+    const int lp = tile_log_p(d);
+    const bool compiled = (d.tile == TileMode::Prefetch && d.tile_w == 16 && lp == 5 &&
                            (d.log_n == 9 || d.log_n == 10)) ||
-                          (d.tile == TileMode::Tma && d.tile_w == 4 && d.log_n == 11);
+                          (d.tile == TileMode::Tma && d.tile_w == 4 && d.log_n == 11 && lp == 4);
+    if (lp != plan_log_p(d.log_n) && !(lp == 5 && tile_p32_table(d.log_n))) return -92;
     return compiled ? 0 : -85;
   }
   if (d.kind == PassKind::RowsT) {
@@ -205,9 +207,11 @@ int check_tile_pass(const PassDesc& d) {
     if ((((int64_t)1 << a.log_w) % d.tile_w) != 0) return -86;
     if (a.in_c % 2 != 0 || a.in_o % 2 != 0 || a.in_j % 2 != 0) return -87;
     if (d.tile == TileMode::Tma && (a.out_o % a.out_e != 0 || a.out_j % a.out_e != 0)) return -88;
+    const int lp = tile_log_p(d);
     const bool compiled = (d.tile == TileMode::Prefetch && d.tile_w == 8 &&
-                           (d.log_n == 10 || d.log_n == 11)) ||
-                          (d.tile == TileMode::Tma && d.tile_w == 4 && d.log_n == 12);
+                           ((d.log_n == 10 && lp == 5) || (d.log_n == 11 && lp == 4))) ||
+                          (d.tile == TileMode::Tma && d.tile_w == 4 && d.log_n == 12 && lp == 4);
+    if (lp != plan_log_p(d.log_n) && !(lp == 5 && tile_p32_table(d.log_n))) return -92;
     return compiled ? 0 : -89;
   }
   return -90;
