@@ -61,6 +61,8 @@ def emulator():
     lib.emu_fft_2d_dist_layout.restype = ctypes.c_int
     lib.emu_fft_2d_dist_p2p.argtypes = lib.emu_fft_2d_dist_layout.argtypes
     lib.emu_fft_2d_dist_p2p.restype = ctypes.c_int
+    lib.emu_group_lp.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+    lib.emu_group_lp.restype = ctypes.c_int
     lib.emu_plan_1d_passes.argtypes = [ctypes.c_int]
     lib.emu_plan_1d_passes.restype = ctypes.c_int
     return lib

@@ -27,9 +27,9 @@ using namespace ferrum;
 
 namespace {
 
-template <int LOGN>
+template <int LOGN, int LOGP_ = plan_log_p(LOGN)>
 struct Group {
-  static constexpr int LOGP = plan_log_p(LOGN);
+  static constexpr int LOGP = LOGP_;
   using G = Geom<LOGN, LOGP>;
   struct Regs {
     float2 v[G::P];
@@ -305,6 +305,25 @@ int emu_fft_1d(float* data, int log_n, int64_t batch, int direction, int normali
   std::vector<float2> ws(pl.ws_elems);
   float2* d = (float2*)data;
   return run_plan(pl, d, d, ws.data());
+}
+
+// One forward transform of length 2^log_n in place with 2^log_p values per
+// thread and that split's stage tables: the 32-value split the tile kernels
+// run at lengths 2^9..2^12 (tile_p32_table).
+int emu_group_lp(float* data, int log_n, int log_p) {
+  std::vector<float2> tw;
+  append_stage_tables(tw, log_n, log_p);
+  tw.push_back(make_float2(1.f, 0.f));
+  float2* d = (float2*)data;
+  switch (log_n * 8 + log_p) {
+#define X(L, P) \
+  case L * 8 + P: \
+    return Group<L, P>::run(d, d, tw.data());
+    X(9, 5) X(10, 5) X(11, 5) X(12, 5)
+#undef X
+    default:
+      return -1;
+  }
 }
 
 // Number of passes the plan for this 1D size uses (for the tests).

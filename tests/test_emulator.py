@@ -34,6 +34,17 @@ def test_single_pass_matches_oracle(emulator, oracle_mod, log_n, direction, norm
     assert max_rel_err(y, ref) < TOL
 
 
+@pytest.mark.parametrize("log_n,log_p", [(9, 5), (10, 5), (11, 5), (12, 5)])
+def test_tile_value_splits_match_oracle(emulator, oracle_mod, log_n, log_p):
+    # the tile kernels run these lengths with 32 values per thread
+    rng = np.random.default_rng(700 + 8 * log_n + log_p)
+    x = rand_c64(rng, 1 << log_n)
+    y = x.copy()
+    assert emulator.emu_group_lp(y.ctypes.data, log_n, log_p) == 0
+    ref = oracle_mod.fft_1d(x, log_n, "forward", False)
+    assert max_rel_err(y, ref) < TOL
+
+
 @pytest.mark.parametrize("log_n", [15, 16, 17, 18, 20, 21, 22, 23, 24])
 @pytest.mark.parametrize("direction,normalize", [("forward", False), ("inverse", True)])
 def test_multi_pass_matches_oracle(emulator, oracle_mod, log_n, direction, normalize):
