@@ -115,13 +115,16 @@ fft_rows_kernel(const float2* in, float2* out, const float2* __restrict__ tw, in
     if (log_block >= LOGN) {  // unblocked store (the blocked one keeps the direct path)
       const int64_t base = (int64_t)blockIdx.x * C::TILE;
       const int64_t total = nfft * G::N;
+      // The copy stays a plain load/store loop; the input's conjugate is
+      // taken as each thread reads its own values (conjugating inside the
+      // copy halved the N = 16 inverse: 0.318 vs 0.159 ms per 512 MiB).
 #pragma unroll
       for (int i = threadIdx.x; i < C::TILE; i += C::THREADS)
-        smem[tile_pad(i)] = base + i < total ? conj_if(ld_stream(in + base + i), CONJ_IN)
-                                             : make_float2(0.f, 0.f);
+        smem[tile_pad(i)] = base + i < total ? ld_stream(in + base + i) : make_float2(0.f, 0.f);
       __syncthreads();
 #pragma unroll
-      for (int m = 0; m < G::P; ++m) v[m] = smem[tile_pad(g * G::N + t + G::T * m)];
+      for (int m = 0; m < G::P; ++m)
+        v[m] = conj_if(smem[tile_pad(g * G::N + t + G::T * m)], CONJ_IN);
       __syncthreads();  // the exchange regions overlay the tile
       run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
       __syncthreads();
