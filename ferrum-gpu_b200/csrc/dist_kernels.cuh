@@ -69,7 +69,7 @@ fft_rows_scatter_kernel(const float2* __restrict__ in, PeerPtrs dst, const float
   if (valid) {
     const float2* src = in + f * G::N + t;
 #pragma unroll
-    for (int m = 0; m < G::P; ++m) v[m] = conj_if(ld_stream(src + G::T * m), CONJ_IN);
+    for (int m = 0; m < G::P; ++m) v[m] = swap_if(ld_stream(src + G::T * m), CONJ_IN);
   } else {
 #pragma unroll
     for (int m = 0; m < G::P; ++m) v[m] = make_float2(0.f, 0.f);

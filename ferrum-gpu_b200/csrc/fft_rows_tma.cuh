@@ -90,7 +90,7 @@ fft_rows_pf_kernel(const float2* __restrict__ in, float2* out, const float2* __r
     float2 v[G::P];
     const float2* src = xchg + g * G::N + t;  // the tile, unpadded
 #pragma unroll
-    for (int m = 0; m < G::P; ++m) v[m] = conj_if(src[G::T * m], CONJ_IN);
+    for (int m = 0; m < G::P; ++m) v[m] = swap_if(src[G::T * m], CONJ_IN);
     __syncthreads();  // tile reads done before the first exchange writes
     const int64_t next = tile + gridDim.x;
     auto prefetch = [&]() {

@@ -151,7 +151,7 @@ fft_rows_t_tile_kernel(const float2* in, float2* out, const float2* __restrict__
     {
       const float2* src = row_src(tile * W + g) + t;
 #pragma unroll
-      for (int m = 0; m < G::P; ++m) v[m] = conj_if(ld_stream(src + G::T * m), CONJ_IN);
+      for (int m = 0; m < G::P; ++m) v[m] = swap_if(ld_stream(src + G::T * m), CONJ_IN);
     }
     // Exchanges within the row's own warps, the last one regrouped so that
     // the lanes run over the tile's rows for the store.
@@ -269,7 +269,7 @@ fft_cols_tma_kernel(const float2* __restrict__ tw, PassArgs a, int64_t ntiles,
     phase ^= 1u;
     float2 v[G::P];
 #pragma unroll
-    for (int m = 0; m < G::P; ++m) v[m] = conj_if(buf[(t + G::T * m) * W + cl], CONJ_IN);
+    for (int m = 0; m < G::P; ++m) v[m] = swap_if(buf[(t + G::T * m) * W + cl], CONJ_IN);
     __syncthreads();  // the tile is in registers; the exchanges reuse the buffer
     run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncBlock{});
     if constexpr (TW != 0) {
@@ -338,7 +338,7 @@ fft_rows_t_tma_kernel(const float2* in, const float2* __restrict__ tw, RowsTArgs
     {
       const float2* src = row_src(tile * W + g) + t;
 #pragma unroll
-      for (int m = 0; m < G::P; ++m) v[m] = conj_if(ld_stream(src + G::T * m), CONJ_IN);
+      for (int m = 0; m < G::P; ++m) v[m] = swap_if(ld_stream(src + G::T * m), CONJ_IN);
     }
     if (threadIdx.x == 0) bulk_wait_read_all();  // the previous tile's store has read the buffer
     __syncthreads();

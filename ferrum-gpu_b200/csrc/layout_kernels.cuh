@@ -35,7 +35,7 @@ fft_rows_split_kernel(const float* __restrict__ in_re, const float* __restrict__
     // memory, so the two float streams are read and written lane-contiguous.
     const int64_t base = (int64_t)blockIdx.x * C::TILE;
     const int64_t total = nfft * G::N;
-    // (the input's conjugate taken on the read-out, as in fft_rows_kernel)
+    // (the inverse's input step applied on the read-out, as in fft_rows_kernel)
 #pragma unroll
     for (int i = threadIdx.x; i < C::TILE; i += C::THREADS)
       smem[tile_pad(i)] = base + i < total
@@ -44,7 +44,7 @@ fft_rows_split_kernel(const float* __restrict__ in_re, const float* __restrict__
     __syncthreads();
 #pragma unroll
     for (int m = 0; m < G::P; ++m)
-      v[m] = conj_if(smem[tile_pad(g * G::N + t + G::T * m)], CONJ_IN);
+      v[m] = swap_if(smem[tile_pad(g * G::N + t + G::T * m)], CONJ_IN);
     __syncthreads();
     run_stages<LOGN, LOGP, 0>(v, sm, t, tw, SyncWarp{});
     __syncthreads();
@@ -64,7 +64,7 @@ fft_rows_split_kernel(const float* __restrict__ in_re, const float* __restrict__
       const int64_t o = f * G::N + t;
 #pragma unroll
       for (int m = 0; m < G::P; ++m)
-        v[m] = conj_if(make_float2(__ldcs(in_re + o + G::T * m), __ldcs(in_im + o + G::T * m)),
+        v[m] = swap_if(make_float2(__ldcs(in_re + o + G::T * m), __ldcs(in_im + o + G::T * m)),
                        CONJ_IN);
     } else {
 #pragma unroll
