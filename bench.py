@@ -74,6 +74,11 @@ def parse_args():
                          "images (the 2D config); GB/s count 2 passes per transform")
     ap.add_argument("--batch", type=int, default=None,
                     help="transforms per GPU (default 2 GiB / N; smaller only for profiling)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="instead of the bench step: every 1D length 2^2..2^26 and every 2D size "
+                         "64^2..16384^2 on 2 GiB, forward and inverse (1/N), min of 3 rounds of 10 "
+                         "calls, with cuFFT on the same buffers and the error of one transform "
+                         "against complex128; one GPU, one JSON line")
     args = ap.parse_args()
     if args.kind == "2d" and args.log_n > 14:
         ap.error("--kind 2d needs --log-n <= 14")
@@ -688,8 +693,59 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_sweep(args) -> None:
+    """The full-range table: one GPU, 2^28 complex values per buffer. GB/s count
+    16 B per element per pass, 1 pass up to 2^14 and 2 beyond and for 2D."""
+    import torch
+
+    from ferrum_gpu import capi
+
+    torch.cuda.set_device(0)
+    dev = capi.DeviceHandle(0)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.complex(torch.rand(TOTAL_ELEMS, device="cuda", generator=g) * 2 - 1,
+                      torch.rand(TOTAL_ELEMS, device="cuda", generator=g) * 2 - 1)
+    y = torch.empty_like(x)
+    out = {}
+    for kind, sizes in (("1d", range(2, 27)), ("2d", range(6, 15))):
+        fft = capi.fft_1d if kind == "1d" else capi.fft_2d
+        for log_n in sizes:
+            n = 1 << log_n
+            batch = TOTAL_ELEMS // elems_per_item(log_n, kind)
+            fwd = lambda: fft(dev, x.data_ptr(), y.data_ptr(), log_n, batch, "forward", False, sp)
+            inv = lambda: fft(dev, y.data_ptr(), x.data_ptr(), log_n, batch, "inverse", True, sp)
+            f = min(_time_ms(fwd, stream, 10, 3) for _ in range(3))
+            i = min(_time_ms(inv, stream, 10, 3) for _ in range(3))
+            fwd()
+            m = n * n if kind == "2d" else n
+            xs = x[:m].to(torch.complex128)
+            ref = torch.fft.fft2(xs.view(n, n)).reshape(-1) if kind == "2d" else torch.fft.fft(xs)
+            err = float((y[:m].to(torch.complex128) - ref).abs().max() / ref.abs().max())
+            del xs, ref
+            cf, ci = _cufft_fns(x, y, batch, log_n, kind)
+            c_f = _time_ms(cf, stream, 10, 3)
+            c_i = _time_ms(ci, stream, 10, 3)  # wrote x: a well-scaled input for the next size
+            passes = passes_counted(kind, log_n)
+            gbs = lambda ms: round(passes * 16 * TOTAL_ELEMS / (ms * 1e-3) / 1e9, 1)
+            rec = {"batch": batch, "ms": round(f, 4), "inverse_ms": round(i, 4), "GB/s": gbs(f),
+                   "inverse_GB/s": gbs(i), "cufft_ms": round(c_f, 4), "cufft_inverse_ms": round(c_i, 4),
+                   "vs_cufft": round(c_f / f, 3), "vs_cufft_inverse": round(c_i / i, 3),
+                   "max_rel_err_vs_complex128": err}
+            out[f"{kind}_2^{log_n}"] = rec
+            print(f"{kind} 2^{log_n:2d} x{batch:<9d} {f:.4f} / {i:.4f} ms  {rec['GB/s']:7.1f} / "
+                  f"{rec['inverse_GB/s']:7.1f} GB/s  vs cuFFT {rec['vs_cufft']:.2f} / "
+                  f"{rec['vs_cufft_inverse']:.2f}  err {err:.1e}", file=sys.stderr, flush=True)
+    print(json.dumps({"sweep": out, "unit": "GB/s", "data": "synthetic uniform[-1,1)",
+                      "bytes_per_buffer": TOTAL_ELEMS * 8}))
+
+
 def main():
     args = parse_args()
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
