@@ -138,9 +138,12 @@ const Tables& tables() {
   return t;
 }
 
-float2 conj_if(float2 v, bool c) { return c ? make_float2(v.x, -v.y) : v; }
+// The inverse's input and output steps as the kernels take them
+// (fft_kernels.cuh swap_if / epilogue): real and imaginary parts swapped,
+// which over the whole transform equals conjugating both ends.
+float2 conj_if(float2 v, bool c) { return c ? make_float2(v.y, v.x) : v; }
 float2 epi(float2 v, bool conj_out, float scale) {
-  return conj_out ? make_float2(v.x * scale, -v.y * scale) : v;
+  return conj_out ? make_float2(v.y * scale, v.x * scale) : v;
 }
 
 // fft_cols_l2_kernel: per tile of W columns, sub-pass 1 (units a < A) into
@@ -374,7 +377,7 @@ int emu_fft_2d_dist_p2p(float* data, int log_n, int nranks, int direction, int n
       for (int64_t f = 0; f < b; ++f) {
         for (int64_t e = 0; e < n; ++e) {
           const float2 v = in[p][f * n + e];
-          x[e] = inv ? make_float2(v.x, -v.y) : v;  // CONJ_IN of the scatter kernel
+          x[e] = conj_if(v, inv);  // CONJ_IN of the scatter kernel
         }
         if (int rc = run_group(log_n, x.data(), x.data(), stw)) return rc;
         for (int64_t e = 0; e < n; ++e)
