@@ -5,7 +5,8 @@
 // Every pass reads and writes each element once, with row segments of at
 // least 64-128 bytes:
 //   * 1D, N <= 2^14: one fft_rows_kernel pass.
-//   * 1D, 2^15..2^23: two passes, N = N1*N2, x[n2 + N2*n1]:
+//   * 1D, 2^15..2^23: two passes, N = N1*N2 (N1 = 2^(log_n/2), except
+//     2^22 = 1024 x 4096), x[n2 + N2*n1]:
 //       A  DFT over n1 (columns of the N1 x N2 view), times W_N^(n2*k1);
 //       B  DFT over n2 (rows), stored transposed to X[k1 + N1*k2].
 //     (2^19..2^23 run both passes in the persistent tile kernels).
@@ -192,6 +193,14 @@ inline int64_t cols_l2_ws_elems(int log_n) {
 // Passes of a multi-pass 1D transform.
 inline int plan_1d_passes(int log_n) { return log_n <= kMaxSinglePassLogN ? 1 : (log_n <= 23 ? 2 : 3); }
 
+// Column length 2^l1 of the two-pass split N = N1 * N2: half of log_n, except
+// 2^22 = 1024 x 4096, which takes the 16-column tiles of the 1024-point
+// column pass and the 4096-point transposed-row pass instead of the 4-column
+// (32-byte segment) 2048-point column pass (per 512 MiB: 0.210 + 0.214 vs
+// 0.250 + 0.194 ms; the whole 2 GiB transform 1.731 -> 1.678 ms forward,
+// 1.791 -> 1.759 inverse on one B200).
+inline int four_step_split_l1(int log_n) { return log_n == 22 ? 10 : log_n / 2; }
+
 // Kernels of the two passes of the 2^19..2^23 transforms: per pass the tile
 // kernel family and the tile width (transforms per tile), chosen by measured
 // per-pass time on B200 (512 MiB batches, per pass in ms: the plain strided
@@ -242,7 +251,7 @@ inline PassPlan plan_1d(int log_n, int64_t batch, bool inv, bool normalize) {
   }
   pl.ws_elems = n * batch;
   if (np == 2) {
-    const int l1 = log_n / 2, l2 = log_n - l1;
+    const int l1 = four_step_split_l1(log_n), l2 = log_n - l1;
     const int64_t n1 = (int64_t)1 << l1, n2 = (int64_t)1 << l2;
     PassArgs a = pass_args(batch * n2, l2, 0, n, 0, n2, n, 0, n2);
     a.tc = 1;

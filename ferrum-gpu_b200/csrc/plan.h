@@ -68,13 +68,9 @@ FERRUM_HD constexpr bool tile_p32_table(int log_n) { return log_n >= 9 && log_n 
 
 // Largest single-pass length (one HBM read + one HBM write per element).
 constexpr int kMaxSinglePassLogN = 14;
-// Largest 1D length (four-step, two passes).
+// Largest 1D length (multi-pass; the pass splits are in passes.h).
 constexpr int kMaxLogN = 26;
 // Split of the four-step twiddle exponent: W_N^e = HI[e >> 12] * LO[e & 4095].
 constexpr int kFourStepLoBits = 12;
-
-// Four-step split N = N1 * N2 (N1 = column FFT length, N2 = row FFT length).
-FERRUM_HD constexpr int four_step_log_n1(int log_n) { return log_n / 2; }
-FERRUM_HD constexpr int four_step_log_n2(int log_n) { return log_n - log_n / 2; }
 
 }  // namespace ferrum
