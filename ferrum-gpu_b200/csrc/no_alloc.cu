@@ -1,8 +1,9 @@
 // Allocation-free 1D entry point: ferrum_fft_1d_c2c_pow2_noalloc.
 //
-// Lengths above 2^14 run the multi-pass transform (two passes up to 2^21,
-// three from 2^22), whose passes keep an N*batch intermediate in scratch
-// memory. ferrum_fft_1d_c2c_pow2 takes that scratch
+// Lengths above 2^14 run the multi-pass transform (two passes up to 2^23,
+// three from 2^24), whose passes keep an N*batch intermediate in scratch
+// memory; with at most 2^22 values here, only the two-pass plans (2^15..2^22)
+// reach the scratch. ferrum_fft_1d_c2c_pow2 takes that scratch
 // from a stream-ordered pool and ferrum_fft_1d_c2c_pow2_ws from the caller;
 // this entry point instead uses one file-scope __device__ array, so the call
 // itself never allocates device memory. It exists for callers that cannot

@@ -7,7 +7,7 @@ device array instead of a workspace. Calls in a row (different lengths, so
 each later call sees the previous call's leftovers in the shared array) must
 match the pool-backed entry point ferrum_fft_1d_c2c_pow2 within the suite's
 1e-4 tolerance; the largest case (one 2^22 transform, the whole scratch and
-the longest plan) is also compared with the CPU oracle directly. A request
+the longest length it takes) is also compared with the CPU oracle directly. A request
 larger than the array, or a batch whose size would overflow, is rejected.
 """
 
@@ -46,7 +46,7 @@ def test_no_alloc_matches_pool_entry_point(oracle_mod):
     try:
         cases = [(20, 4, "forward", False),   # fills the whole 2^22 scratch
                  (18, 3, "inverse", True),    # second call over stale contents
-                 (22, 1, "forward", False),   # the longest plan, whole scratch again
+                 (22, 1, "forward", False),   # the longest length, whole scratch again
                  (12, 5, "forward", False)]   # single pass, no scratch
         for i, (log_n, batch, direction, normalize) in enumerate(cases):
             x = rand_c64(np.random.default_rng(77 + i), batch << log_n, "normal")
